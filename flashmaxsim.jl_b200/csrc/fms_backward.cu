@@ -1,0 +1,421 @@
+// fms_backward.cu -- sparse MaxSim backward from the argmax tape (Eqs. 2-3):
+//   dQ[:,t] = sum over units using query token t of  delta_u * D[:, u*]
+//   dD[:,u] = sum over (unit, t) whose argmax is u of delta_u * Q[:, t]
+// with delta_u = T(Delta[u] * inv_n[q(u)]) formed in T (rrule.jl:77,94,112;
+// backward_layouts.jl:19,79,146).  Two strategies, as the reference's
+// BackwardStrategy (types.jl:8-17):
+//  * AtomicUnified (kernels_backward.jl:69-138): one fused launch; a warp per
+//    query token walks the units that use it, gathers dQ in registers and
+//    scatters dD with float32 atomics (into dD directly for f32/f64, into a
+//    float32 workspace then one conversion pass for 16-bit T).
+//  * InvGrid (kernels_backward.jl:146-354, csr_ka.jl): inverse-grid CSR built
+//    by a parallel counting sort (atomic count -> block-parallel exclusive scan,
+//    replacing the reference's one-thread serial prefix -> atomic fill), then a
+//    destination-owned scatter: a warp per document token sums its sources in
+//    ascending source order (segments up to 1024 sources are ranked in shared
+//    memory), so dD is deterministic run to run, unlike the reference's
+//    atomic-order fill.  The dQ gather is the same warp-per-token kernel.
+// Accumulation is float32 (float64 for T = Float64) and each gradient element
+// is rounded to T once.
+#include "fms_common.cuh"
+#include "fms_internal.h"
+
+namespace fms {
+
+// Units that read query-token row r: a contiguous id range [u0, u0+cnt).
+__device__ inline void units_of_row(const ScanParams& p, int64_t r, int64_t& u0, int64_t& cnt,
+                                    int& t) {
+  switch (p.layout) {
+    case L_PAIRED: t = (int)(r % p.Tq); u0 = r / p.Tq; cnt = 1; break;
+    case L_CANDIDATES: t = (int)(r % p.Tq); u0 = (r / p.Tq) * p.C; cnt = p.C; break;
+    case L_INBATCH: t = (int)(r % p.Tq); u0 = (r / p.Tq) * p.Bd; cnt = p.Bd; break;
+    case L_PACKED: t = (int)(r % p.Tq); u0 = (r / p.Tq) * p.B; cnt = p.B; break;
+    default: {  // varlen: binary search cu_q for the pair owning token row r
+      int lo = 0, hi = p.N;  // find n with cu_q[n]-1 <= r < cu_q[n+1]-1
+      while (hi - lo > 1) {
+        int mid = (lo + hi) >> 1;
+        if ((int64_t)p.cu_q[mid] - 1 <= r) lo = mid; else hi = mid;
+      }
+      u0 = lo; cnt = (p.N > 0) ? 1 : 0;
+      t = (int)(r - ((int64_t)p.cu_q[lo] - 1));
+      break;
+    }
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ typename Tr<T>::Acc unit_delta(const BwdParams& b, int64_t u, int qidx) {
+  using A = typename Tr<T>::Acc;
+  const T* Dl = static_cast<const T*>(b.Delta);
+  A d = Tr<T>::to(Dl[u]);
+  if (b.inv_n) d = tmul<T>(d, Tr<T>::to(static_cast<const T*>(b.inv_n)[qidx]));
+  return d;
+}
+
+constexpr int BW_VEC = 8;              // dim elements per lane per chunk
+constexpr int BW_CHUNK = 32 * BW_VEC;  // dim elements per warp chunk
+
+// Warp per query-token row: dQ gather (+ dD atomics when ATOMIC).
+template <typename T, bool ATOMIC>
+__global__ void __launch_bounds__(256) bwd_gather_kernel(BwdParams b, typename Tr<T>::Acc* dD_acc) {
+  using A = typename Tr<T>::Acc;
+  const ScanParams& p = b.g;
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const T* Q = static_cast<const T*>(p.Q);
+  const T* D = static_cast<const T*>(p.D);
+  T* dQ = static_cast<T*>(b.dQ);
+  const int dim = p.dim;
+  for (int64_t r = warp; r < b.nq_rows; r += nwarps) {
+    int64_t u0, cnt;
+    int t;
+    units_of_row(p, r, u0, cnt, t);
+    for (int k0 = 0; k0 < dim; k0 += BW_CHUNK) {
+      A acc[BW_VEC];
+      A qv[BW_VEC];
+#pragma unroll
+      for (int v = 0; v < BW_VEC; ++v) {
+        acc[v] = (A)0;
+        int k = k0 + lane + 32 * v;
+        qv[v] = (ATOMIC && k < dim) ? Tr<T>::to(Q[r * dim + k]) : (A)0;
+      }
+      for (int64_t i = 0; i < cnt; ++i) {
+        int64_t u = u0 + i;
+        Unit U = decode_unit(p, u);
+        if (!U.valid || t >= U.Tq || !mask_ok(U.qmask, t)) continue;
+        int a = p.args[U.arg0 + t];
+        if (a < 1 || a > U.Td) continue;
+        A dl = unit_delta<T>(b, u, U.qidx);
+        int64_t drow = U.d0 + a - 1;
+#pragma unroll
+        for (int v = 0; v < BW_VEC; ++v) {
+          int k = k0 + lane + 32 * v;
+          if (k < dim) {
+            acc[v] += dl * Tr<T>::to(D[drow * dim + k]);
+            if (ATOMIC) atomicAdd(&dD_acc[drow * dim + k], dl * qv[v]);
+          }
+        }
+      }
+#pragma unroll
+      for (int v = 0; v < BW_VEC; ++v) {
+        int k = k0 + lane + 32 * v;
+        if (k < dim) dQ[r * dim + k] = Tr<T>::from(acc[v]);
+      }
+    }
+  }
+}
+
+template <typename A, typename T>
+__global__ void convert_kernel(const A* __restrict__ src, T* __restrict__ dst, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    dst[i] = Tr<T>::from(src[i]);
+}
+
+// ------------------------------------------------------------------ InvGrid CSR
+
+// Sources are (unit, t) pairs, id = unit * Tq + t (Tq = max_q for varlen).
+__device__ __forceinline__ bool source_dest(const ScanParams& p, int64_t s, int64_t& dest) {
+  int64_t u = s / p.Tq;
+  int t = (int)(s % p.Tq);
+  Unit U = decode_unit(p, u);
+  if (!U.valid || t >= U.Tq || !mask_ok(U.qmask, t)) return false;
+  int a = p.args[U.arg0 + t];
+  if (a < 1 || a > U.Td) return false;
+  dest = U.d0 + a - 1;
+  return true;
+}
+
+__global__ void csr_count_kernel(ScanParams p, int64_t n_src, int32_t* __restrict__ count) {
+  for (int64_t s = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; s < n_src;
+       s += (int64_t)gridDim.x * blockDim.x) {
+    int64_t dest;
+    if (source_dest(p, s, dest)) atomicAdd(&count[dest], 1);
+  }
+}
+
+constexpr int SCAN_BLOCK = 1024;
+
+// In-place exclusive scan, phase 1: each block scans 1024 entries and records
+// its total.
+__global__ void __launch_bounds__(SCAN_BLOCK) scan_blocks_kernel(int32_t* __restrict__ x, int64_t n,
+                                                                int32_t* __restrict__ block_sums) {
+  __shared__ int32_t warp_sums[32];
+  int64_t i = (int64_t)blockIdx.x * SCAN_BLOCK + threadIdx.x;
+  int32_t v = (i < n) ? x[i] : 0;
+  int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  int32_t incl = v;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    int32_t o = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= off) incl += o;
+  }
+  if (lane == 31) warp_sums[w] = incl;
+  __syncthreads();
+  if (w == 0) {
+    int32_t ws = warp_sums[lane];
+    int32_t wi = ws;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      int32_t o = __shfl_up_sync(0xffffffffu, wi, off);
+      if (lane >= off) wi += o;
+    }
+    warp_sums[lane] = wi - ws;  // exclusive warp offsets
+    if (lane == 31) block_sums[blockIdx.x] = wi;
+  }
+  __syncthreads();
+  if (i < n) x[i] = incl - v + warp_sums[w];
+}
+
+// Phase 2: one block scans the block totals sequentially in chunks of 1024.
+__global__ void __launch_bounds__(SCAN_BLOCK) scan_sums_kernel(int32_t* __restrict__ sums, int64_t nb) {
+  __shared__ int32_t warp_sums[32];
+  __shared__ int32_t carry;
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  for (int64_t base = 0; base < nb; base += SCAN_BLOCK) {
+    int64_t i = base + threadIdx.x;
+    int32_t v = (i < nb) ? sums[i] : 0;
+    int32_t incl = v;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      int32_t o = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += o;
+    }
+    if (lane == 31) warp_sums[w] = incl;
+    __syncthreads();
+    if (w == 0) {
+      int32_t ws = warp_sums[lane];
+      int32_t wi = ws;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        int32_t o = __shfl_up_sync(0xffffffffu, wi, off);
+        if (lane >= off) wi += o;
+      }
+      warp_sums[lane] = wi - ws;
+    }
+    __syncthreads();
+    int32_t c = carry;
+    if (i < nb) sums[i] = incl - v + warp_sums[w] + c;
+    __syncthreads();
+    if (threadIdx.x == SCAN_BLOCK - 1) carry = c + incl + warp_sums[w];
+    __syncthreads();
+  }
+}
+
+// Phase 3: add block offsets; also seed the fill cursors.
+__global__ void scan_add_kernel(int32_t* __restrict__ x, int64_t n, const int32_t* __restrict__ sums,
+                                int32_t* __restrict__ cursor, int64_t n_dest) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int32_t v = x[i] + sums[i / SCAN_BLOCK];
+    x[i] = v;
+    if (i < n_dest) cursor[i] = v;
+  }
+}
+
+__global__ void csr_fill_kernel(ScanParams p, int64_t n_src, int32_t* __restrict__ cursor,
+                                int32_t* __restrict__ col_idx) {
+  for (int64_t s = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; s < n_src;
+       s += (int64_t)gridDim.x * blockDim.x) {
+    int64_t dest;
+    if (source_dest(p, s, dest)) {
+      int32_t pos = atomicAdd(&cursor[dest], 1);
+      col_idx[pos] = (int32_t)s;
+    }
+  }
+}
+
+constexpr int SC_WARPS = 8;
+constexpr int SC_SEG = 1024;  // sources ranked per destination in shared memory
+
+// Warp per destination document token; sources summed in ascending id order.
+template <typename T>
+__global__ void __launch_bounds__(SC_WARPS * 32)
+csr_scatter_kernel(BwdParams b, const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col_idx) {
+  using A = typename Tr<T>::Acc;
+  __shared__ int32_t seg_s[SC_WARPS][SC_SEG];
+  const ScanParams& p = b.g;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  int32_t* seg = seg_s[w];
+  const T* Q = static_cast<const T*>(p.Q);
+  T* dD = static_cast<T*>(b.dD);
+  const int dim = p.dim;
+  const int64_t warp = (int64_t)blockIdx.x * SC_WARPS + w;
+  const int64_t nwarps = (int64_t)gridDim.x * SC_WARPS;
+  for (int64_t d = warp; d < b.nd_rows; d += nwarps) {
+    const int32_t a0 = row_ptr[d], n = row_ptr[d + 1] - a0;
+    const bool ranked = n <= SC_SEG;
+    if (ranked) {
+      // rank each source id by counting smaller ids (ids are distinct)
+      for (int i = lane; i < n; i += 32) {
+        int32_t x = col_idx[a0 + i];
+        int r = 0;
+        for (int j = 0; j < n; ++j) r += (col_idx[a0 + j] < x) ? 1 : 0;
+        seg[r] = x;
+      }
+      __syncwarp();
+    }
+    for (int k0 = 0; k0 < dim; k0 += BW_CHUNK) {
+      A acc[BW_VEC];
+#pragma unroll
+      for (int v = 0; v < BW_VEC; ++v) acc[v] = (A)0;
+      for (int i = 0; i < n; ++i) {
+        int64_t s = ranked ? seg[i] : col_idx[a0 + i];
+        int64_t u = s / p.Tq;
+        int t = (int)(s % p.Tq);
+        Unit U = decode_unit(p, u);
+        A dl = unit_delta<T>(b, u, U.qidx);
+        int64_t qrow = U.q0 + t;
+#pragma unroll
+        for (int v = 0; v < BW_VEC; ++v) {
+          int k = k0 + lane + 32 * v;
+          if (k < dim) acc[v] += dl * Tr<T>::to(Q[qrow * dim + k]);
+        }
+      }
+#pragma unroll
+      for (int v = 0; v < BW_VEC; ++v) {
+        int k = k0 + lane + 32 * v;
+        if (k < dim) dD[d * dim + k] = Tr<T>::from(acc[v]);
+      }
+    }
+    __syncwarp();
+  }
+}
+
+static inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+size_t bwd_workspace_bytes(int strategy, int dtype, int64_t n_src, int64_t n_dest,
+                           int64_t grad_d_numel) {
+  if (strategy == FMS_ATOMIC_UNIFIED) {
+    if (dtype == FMS_F16 || dtype == FMS_BF16) return align_up((size_t)grad_d_numel * 4, 256);
+    return 0;
+  }
+  size_t nscan = (size_t)n_dest + 1;
+  size_t nb = (nscan + SCAN_BLOCK - 1) / SCAN_BLOCK;
+  return align_up(nscan * 4, 256) + align_up((size_t)n_dest * 4 + 4, 256) +
+         align_up((size_t)n_src * 4 + 4, 256) + align_up(nb * 4 + 4, 256);
+}
+
+template <typename T>
+static cudaError_t run_backward(int strategy, const BwdParams& b, void* ws, size_t ws_bytes,
+                                cudaStream_t s) {
+  using A = typename Tr<T>::Acc;
+  const ScanParams& p = b.g;
+  const int sms = device_sm_count();
+  const int64_t dim = p.dim;
+  cudaError_t e;
+  auto grid_for = [&](int64_t work, int per_block) -> unsigned {
+    int64_t g = (work + per_block - 1) / per_block;
+    int64_t cap = (int64_t)sms * 32;
+    if (g > cap) g = cap;
+    return (unsigned)(g < 1 ? 1 : g);
+  };
+  if (strategy == FMS_ATOMIC_UNIFIED) {
+    A* acc = nullptr;
+    const bool wide = sizeof(T) == sizeof(A);
+    if (wide) {
+      acc = reinterpret_cast<A*>(b.dD);
+    } else {
+      if (ws == nullptr || ws_bytes < (size_t)b.nd_rows * dim * sizeof(A)) return cudaErrorInvalidValue;
+      acc = reinterpret_cast<A*>(ws);
+    }
+    e = cudaMemsetAsync(acc, 0, (size_t)b.nd_rows * dim * sizeof(A), s);
+    if (e != cudaSuccess) return e;
+    bwd_gather_kernel<T, true><<<grid_for(b.nq_rows, 8), 256, 0, s>>>(b, acc);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    if (!wide) {
+      int64_t n = b.nd_rows * dim;
+      convert_kernel<A, T><<<grid_for(n, 256), 256, 0, s>>>(acc, static_cast<T*>(b.dD), n);
+      if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+  }
+  // InvGrid
+  const int64_t n_src = p.nunits * (int64_t)p.Tq;
+  const int64_t n_dest = b.nd_rows;
+  const size_t need = bwd_workspace_bytes(strategy, 0, n_src, n_dest, 0);
+  if (ws == nullptr || ws_bytes < need) return cudaErrorInvalidValue;
+  const int64_t nscan = n_dest + 1;
+  const int64_t nb = (nscan + SCAN_BLOCK - 1) / SCAN_BLOCK;
+  char* w = static_cast<char*>(ws);
+  int32_t* row_ptr = reinterpret_cast<int32_t*>(w);
+  w += align_up((size_t)nscan * 4, 256);
+  int32_t* cursor = reinterpret_cast<int32_t*>(w);
+  w += align_up((size_t)n_dest * 4 + 4, 256);
+  int32_t* col_idx = reinterpret_cast<int32_t*>(w);
+  w += align_up((size_t)n_src * 4 + 4, 256);
+  int32_t* sums = reinterpret_cast<int32_t*>(w);
+
+  // dQ gather (no atomics)
+  bwd_gather_kernel<T, false><<<grid_for(b.nq_rows, 8), 256, 0, s>>>(b, nullptr);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  // counting sort: counts land at row_ptr[dest], exclusive scan turns them into
+  // segment starts, row_ptr[n_dest] = nnz.
+  if ((e = cudaMemsetAsync(row_ptr, 0, (size_t)nscan * 4, s)) != cudaSuccess) return e;
+  if (n_src > 0) {
+    csr_count_kernel<<<grid_for(n_src, 256), 256, 0, s>>>(p, n_src, row_ptr);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
+  scan_blocks_kernel<<<(unsigned)nb, SCAN_BLOCK, 0, s>>>(row_ptr, nscan, sums);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  scan_sums_kernel<<<1, SCAN_BLOCK, 0, s>>>(sums, nb);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  scan_add_kernel<<<grid_for(nscan, 256), 256, 0, s>>>(row_ptr, nscan, sums, cursor, n_dest);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  if (n_src > 0) {
+    csr_fill_kernel<<<grid_for(n_src, 256), 256, 0, s>>>(p, n_src, cursor, col_idx);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
+  if (n_dest > 0) {
+    csr_scatter_kernel<T><<<grid_for(n_dest, SC_WARPS), SC_WARPS * 32, 0, s>>>(b, row_ptr, col_idx);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+cudaError_t launch_backward(int dtype, int strategy, const BwdParams& b, void* ws, size_t ws_bytes,
+                            cudaStream_t s) {
+  // zero-size outputs: nothing to do
+  if (b.g.dim == 0) return cudaSuccess;
+  switch (dtype) {
+    case FMS_F32: return run_backward<float>(strategy, b, ws, ws_bytes, s);
+    case FMS_F16: return run_backward<__half>(strategy, b, ws, ws_bytes, s);
+    case FMS_BF16: return run_backward<__nv_bfloat16>(strategy, b, ws, ws_bytes, s);
+    case FMS_F64: return run_backward<double>(strategy, b, ws, ws_bytes, s);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+// ------------------------------------------------------------------ inv counts
+
+template <typename T>
+__global__ void inv_counts_kernel(const uint8_t* __restrict__ qmask, int Tq, int B, T* inv_n) {
+  using A = typename Tr<T>::Acc;
+  int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= B) return;
+  int n = 0;
+  for (int t = 0; t < Tq; ++t) n += (qmask == nullptr || qmask[(int64_t)b * Tq + t]) ? 1 : 0;
+  A c = (A)(n > 1 ? n : 1);
+  inv_n[b] = Tr<T>::from((A)1 / c);
+}
+
+cudaError_t launch_inv_counts(int dtype, const uint8_t* qmask, int Tq, int B, void* inv_n,
+                              cudaStream_t s) {
+  if (B == 0) return cudaSuccess;
+  unsigned g = (unsigned)((B + 127) / 128);
+  switch (dtype) {
+    case FMS_F32: inv_counts_kernel<float><<<g, 128, 0, s>>>(qmask, Tq, B, (float*)inv_n); break;
+    case FMS_F16: inv_counts_kernel<__half><<<g, 128, 0, s>>>(qmask, Tq, B, (__half*)inv_n); break;
+    case FMS_BF16:
+      inv_counts_kernel<__nv_bfloat16><<<g, 128, 0, s>>>(qmask, Tq, B, (__nv_bfloat16*)inv_n);
+      break;
+    case FMS_F64: inv_counts_kernel<double><<<g, 128, 0, s>>>(qmask, Tq, B, (double*)inv_n); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace fms

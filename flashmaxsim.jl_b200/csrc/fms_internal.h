@@ -1,0 +1,35 @@
+// fms_internal.h -- launcher declarations shared between the kernel files and
+// the C-ABI layer (fms_abi.cu).  Not part of the public ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace fms {
+
+struct ScanParams;
+
+// Number of SMs of the current device (cached per device).
+int device_sm_count();
+// Compute capability major*10+minor of the current device (cached per device).
+int device_cc();
+
+// Forward scans.  dtype is an fms_dtype.
+cudaError_t launch_scan_simt(int dtype, const ScanParams& p, cudaStream_t s);
+// tcgen05 + TMA engine for 16-bit features.  Returns cudaErrorNotSupported when
+// the shape or pointers do not meet its TMA constraints (caller falls back to
+// the SIMT scan, which is also a GPU kernel).
+cudaError_t launch_scan_tc(int dtype, const ScanParams& p, cudaStream_t s);
+bool scan_tc_supported(int dtype, const ScanParams& p);
+
+cudaError_t launch_inv_counts(int dtype, const uint8_t* qmask, int Tq, int B, void* inv_n,
+                              cudaStream_t s);
+
+// Backward (all layouts share ScanParams for the geometry).
+struct BwdParams;
+size_t bwd_workspace_bytes(int strategy, int dtype, int64_t n_src, int64_t n_dest,
+                           int64_t grad_d_numel);
+cudaError_t launch_backward(int dtype, int strategy, const BwdParams& b, void* ws,
+                            size_t ws_bytes, cudaStream_t s);
+
+}  // namespace fms

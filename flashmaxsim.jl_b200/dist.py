@@ -1,0 +1,121 @@
+"""Multi-GPU MaxSim: documents sharded by id over the GPUs of one node, one
+process per GPU (torch.distributed, NCCL over NVLink).  The reference is
+single-device; these paths are new.  Only small outputs cross NVLink:
+
+  * candidates: every rank scores the candidate slots whose doc it owns (others
+    get -Inf), then an all-reduce(max) of the (B, C) float32 score matrix merges
+    the owner-disjoint results and `neg` is written into globally invalid slots;
+  * INT8 exhaustive search: every rank keeps its local top-k per query, the
+    (nq, k) lists are all-gathered and merged on the device;
+  * packed scan: contiguous doc ranges per rank, all-gather of the (nq, B_r)
+    score blocks.
+
+The merge functions take the local results as tensors and are independent of
+the kernels, so their host logic is tested with gloo ranks on CPU.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from . import _lib
+from . import layouts as L
+from .errors import ArgumentError, DimensionMismatch
+
+
+def shard_range(n_global: int, world: int, rank: int):
+    """Contiguous 1-based doc-id range [lo, hi] of `rank` (balanced)."""
+    base, extra = divmod(n_global, world)
+    lo = rank * base + min(rank, extra) + 1
+    n = base + (1 if rank < extra else 0)
+    return lo, lo + n - 1
+
+
+def candidates_shard_forward(Q, gallery_shard, idxs, qmask, dmask_shard, shard_lo,
+                             normalize=False):
+    """Scores of the slots this shard owns; -Inf elsewhere (fms_candidates_shard_fwd)."""
+    if Q.dim() != 3 or gallery_shard.dim() != 3:
+        raise DimensionMismatch("candidate layout expects (B, Tq, dim) and (N, Td, dim)")
+    B, Tq, dim = Q.shape
+    N, Td = gallery_shard.shape[0], gallery_shard.shape[1]
+    if gallery_shard.shape[2] != dim:
+        raise DimensionMismatch("feature dim")
+    if idxs.dim() != 2 or idxs.shape[0] != B:
+        raise DimensionMismatch("idxs")
+    dev = L._device_of(Q, gallery_shard, idxs, qmask, dmask_shard)
+    Q, G = L._feat(Q), L._feat(gallery_shard)
+    ix = L._i32(idxs, "idxs")
+    C = ix.shape[1]
+    qm = L._mask(qmask, (B, Tq), "qmask")
+    dm = L._mask(dmask_shard, (N, Td), "dmask")
+    S = torch.empty((B, C), dtype=L.score_dtype(Q.dtype), device=dev)
+    L._run("fms_candidates_shard_fwd", dev, _lib.DTYPE_CODE[Q.dtype], _lib.ptr(Q), _lib.ptr(G),
+           _lib.ptr(ix), _lib.ptr(qm), _lib.ptr(dm), dim, Tq, B, Td, N, C, int(shard_lo),
+           int(normalize), _lib.ptr(S))
+    return S
+
+
+def finalize_neg(idxs, n_global, neg, S):
+    """Write T(neg) into slots whose idx is outside 1:n_global (on the device)."""
+    dev = L._device_of(idxs, S)
+    B, C = S.shape
+    if S.dtype != torch.float32:
+        raise ArgumentError("finalize_neg expects float32 scores")
+    ix = L._i32(idxs, "idxs")
+    L._run("fms_candidates_finalize_neg", dev, _lib.ptr(ix), int(n_global), C, B, float(neg),
+           _lib.ptr(S))
+    return S
+
+
+def merge_candidate_scores(S_local, idxs, n_global, neg, finalize=finalize_neg, group=None):
+    """All-reduce(max) of owner-disjoint shard scores, then the `neg` fill."""
+    if dist.is_initialized() and dist.get_world_size(group) > 1:
+        dist.all_reduce(S_local, op=dist.ReduceOp.MAX, group=group)
+    return finalize(idxs, n_global, neg, S_local)
+
+
+def sharded_candidates(Q, gallery_shard, idxs, qmask, dmask_shard, shard_lo, n_global,
+                       neg=-1.0e4, normalize=False, group=None):
+    """maxsim(Q, gallery, idxs, ...) with the gallery sharded over the group.
+    Returns the full (B, C) scores on every rank."""
+    S = candidates_shard_forward(Q, gallery_shard, idxs, qmask, dmask_shard, shard_lo,
+                                 normalize)
+    negv = L._neg_value(neg, Q.dtype)
+    return merge_candidate_scores(S, idxs, n_global, negv, group=group)
+
+
+def merge_topk(vals, ids, k, merge=None, group=None):
+    """All-gather per-shard (nq, k) top-k lists and merge them (score desc, id asc)."""
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    if world == 1:
+        return vals, ids
+    gv = [torch.empty_like(vals) for _ in range(world)]
+    gi = [torch.empty_like(ids) for _ in range(world)]
+    dist.all_gather(gv, vals.contiguous(), group=group)
+    dist.all_gather(gi, ids.contiguous(), group=group)
+    merge = merge or L.topk_merge
+    return merge(torch.stack(gv), torch.stack(gi), k)
+
+
+def sharded_int8_topk(Q, index_shard, shard_lo, k, qmask=None, dmask_shard=None,
+                      normalize=False, group=None):
+    """Exhaustive INT8 search over an index sharded by doc id: local top-k with
+    global ids, then an NCCL all-gather + device merge."""
+    vals, ids = L.int8_exhaustive_forward(Q, index_shard, qmask, dmask_shard, normalize, topk=k,
+                                          id_offset=shard_lo - 1)
+    return merge_topk(vals, ids, k, group=group)
+
+
+def gather_packed_scores(S_local, counts, group=None):
+    """All-gather (nq, B_r) packed-scan score blocks of contiguous doc ranges into
+    (nq, sum B_r).  counts[r] = docs of rank r."""
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    if world == 1:
+        return S_local
+    nq = S_local.shape[0]
+    mx = max(counts)
+    buf = torch.full((nq, mx), float("nan"), dtype=S_local.dtype, device=S_local.device)
+    buf[:, :S_local.shape[1]] = S_local
+    parts = [torch.empty_like(buf) for _ in range(world)]
+    dist.all_gather(parts, buf, group=group)
+    return torch.cat([p[:, :c] for p, c in zip(parts, counts)], dim=1)

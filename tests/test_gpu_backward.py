@@ -1,0 +1,149 @@
+"""GPU parity of the sparse backward (AtomicUnified and InvGrid) against the
+oracle's CPU pullbacks (backward_*.jl), the closed form (test_math_oracle.jl)
+and autograd through `maxsim` (rrule.jl)."""
+import numpy as np
+import pytest
+import torch
+
+from conftest import l2cols, seeded
+
+pytestmark = pytest.mark.gpu
+
+MODES = [(0, "AtomicUnified"), (1, "InvGrid")]
+DT = {"f32": (torch.float32, 1e-5, 0), "f16": (torch.float16, 2e-3, 1),
+      "bf16": (torch.bfloat16, 1e-2, 2)}
+
+
+def feats(rng, shape, dtype):
+    return torch.from_numpy(l2cols(rng.standard_normal(shape))).to(dtype).cuda()
+
+
+def close(got, ref, rtol, what):
+    g = got.detach().float().cpu().numpy()
+    ref = np.asarray(ref, np.float32)
+    atol = rtol * max(1.0, float(np.abs(ref).max()))
+    np.testing.assert_allclose(g, ref, rtol=rtol, atol=atol, err_msg=what)
+
+
+def strategy(fms, code):
+    return fms.AtomicUnified() if code == 0 else fms.InvGrid()
+
+
+@pytest.mark.parametrize("dt", list(DT))
+@pytest.mark.parametrize("code,name", MODES)
+def test_paired_pullback(fms, oracle, dt, code, name):
+    dtype, tol, dcode = DT[dt]
+    rng = seeded(41)
+    B, Tq, Td, dim = 5, 12, 20, 64
+    Q, D = feats(rng, (B, Tq, dim), dtype), feats(rng, (B, Td, dim), dtype)
+    qm = torch.from_numpy(rng.random((B, Tq)) > 0.2).cuda()
+    _, args = fms.paired_forward(Q, D, qm, None)
+    Delta = torch.randn(B, device="cuda").to(dtype)
+    inv = torch.rand(B, device="cuda").to(dtype) + 0.5
+    dQ, dD = fms.paired_pullback(Delta, Q, D, qm, args, inv, strategy(fms, code))
+    dQo, dDo = oracle.paired_pullback(Delta, inv, Q, D, qm.cpu(), args.cpu(), code, dcode)
+    close(dQ, dQo, tol, f"dQ {name}")
+    close(dD, dDo, tol, f"dD {name}")
+
+
+@pytest.mark.parametrize("dt", list(DT))
+@pytest.mark.parametrize("code,name", MODES)
+def test_inbatch_pullback(fms, oracle, dt, code, name):
+    dtype, tol, dcode = DT[dt]
+    rng = seeded(42)
+    Bq, Bd, Tq, Td, dim = 4, 6, 8, 11, 96
+    Q, D = feats(rng, (Bq, Tq, dim), dtype), feats(rng, (Bd, Td, dim), dtype)
+    qm = torch.from_numpy(rng.random((Bq, Tq)) > 0.2).cuda()
+    dm = torch.from_numpy(rng.random((Bd, Td)) > 0.2).cuda()
+    _, args = fms.inbatch_forward(Q, D, qm, dm)
+    Delta = torch.randn(Bq, Bd, device="cuda").to(dtype)
+    dQ, dD = fms.inbatch_pullback(Delta, Q, D, qm, args, None, strategy(fms, code))
+    dQo, dDo = oracle.inbatch_pullback(Delta, None, Q, D, qm.cpu(), args.cpu(), code, dcode)
+    close(dQ, dQo, tol, f"dQ {name}")
+    close(dD, dDo, tol, f"dD {name}")
+
+
+@pytest.mark.parametrize("code,name", MODES)
+def test_candidates_pullback(fms, oracle, code, name):
+    rng = seeded(43)
+    B, C, Tq, Td, N, dim = 3, 5, 8, 10, 9, 32
+    Q, G = feats(rng, (B, Tq, dim), torch.float32), feats(rng, (N, Td, dim), torch.float32)
+    idxs = torch.from_numpy(rng.integers(0, N + 1, (B, C)).astype(np.int32)).cuda()
+    _, args = fms.candidates_forward(Q, G, idxs)
+    Delta = torch.randn(B, C, device="cuda")
+    dQ, dG = fms.candidates_pullback(Delta, Q, G, idxs, None, args, None, strategy(fms, code))
+    dQo, dGo = oracle.candidates_pullback(Delta, None, Q, G, idxs.cpu(), None, args.cpu(), code)
+    close(dQ, dQo, 1e-5, f"dQ {name}")
+    close(dG, dGo, 1e-5, f"dG {name}")
+
+
+@pytest.mark.parametrize("code,name", MODES)
+def test_packed_and_varlen_pullback(fms, oracle, code, name):
+    rng = seeded(44)
+    dim, Tq = 32, 6
+    docs = [feats(rng, (n, dim), torch.float32) for n in (5, 0, 9, 3)]
+    P = fms.pack_docs(docs)
+    Qs = feats(rng, (2, Tq, dim), torch.float32)
+    _, args = fms.packed_forward(Qs, P)
+    Delta = torch.randn(2, 4, device="cuda")
+    dQ, dP = fms.packed_pullback(Delta, Qs, P, None, args, None, strategy(fms, code))
+    dQo, dPo = oracle.packed_pullback(Delta, None, Qs, P.tokens, P.cu.cpu(), None, args.cpu(),
+                                      code)
+    close(dQ, dQo, 1e-5, f"packed dQ {name}")
+    close(dP, dPo, 1e-5, f"packed dP {name}")
+    qs = [feats(rng, (n, dim), torch.float32) for n in (4, 6, 1)]
+    ds = [feats(rng, (n, dim), torch.float32) for n in (5, 3, 8)]
+    Qp, Dp = fms.pack_pairs(qs, ds)
+    _, vargs = fms.varlen_forward(Qp, Dp)
+    Dl = torch.randn(3, device="cuda")
+    dQv, dDv = fms.varlen_pullback(Dl, Qp, Dp, vargs, None, strategy(fms, code))
+    dQvo, dDvo = oracle.varlen_pullback(Dl, None, Qp.tokens, Dp.tokens, Qp.cu.cpu(), Dp.cu.cpu(),
+                                        vargs.cpu(), code)
+    close(dQv, dQvo, 1e-5, f"varlen dQ {name}")
+    close(dDv, dDvo, 1e-5, f"varlen dD {name}")
+
+
+def test_autograd_through_maxsim(fms, oracle):
+    """Gradients of sum(maxsim(...)) match the closed form (rrule.jl + Eqs. 2-3)."""
+    rng = seeded(45)
+    B, Tq, Td, dim = 3, 8, 11, 16
+    for norm in (False, True):
+        for bw in (fms.AtomicUnified, fms.InvGrid):
+            Q = feats(rng, (B, Tq, dim), torch.float32).requires_grad_()
+            D = feats(rng, (B, Td, dim), torch.float32).requires_grad_()
+            cfg = fms.MaxSim(torch.float32, normalize=norm, backward=bw)
+            out = cfg(Q, D)
+            out.sum().backward()
+            _, args = fms.paired_forward(Q.detach(), D.detach())
+            inv = np.full(B, 1.0 / Tq if norm else 1.0, np.float32)
+            dQo, dDo = oracle.paired_pullback(np.ones(B, np.float32), inv, Q.detach(), D.detach(),
+                                              None, args.cpu(), bw.code)
+            close(Q.grad, dQo, 1e-5, "autograd dQ")
+            close(D.grad, dDo, 1e-5, "autograd dD")
+            # in-batch + candidates + packed autograd run and are finite
+    Q = feats(rng, (B, Tq, dim), torch.float32).requires_grad_()
+    D = feats(rng, (B, Td, dim), torch.float32).requires_grad_()
+    fms.maxsim(Q, D, fms.InBatch(), backward=fms.InvGrid()).sum().backward()
+    assert torch.isfinite(Q.grad).all() and torch.isfinite(D.grad).all()
+
+
+def test_nan_cotangent_propagates(fms):
+    # test_regressions.jl:156-170
+    q = torch.randn(3, 4, device="cuda", requires_grad=True)
+    d = torch.randn(5, 4, device="cuda", requires_grad=True)
+    s = fms.maxsim(q, d)
+    s.backward(torch.tensor([float("nan")], device="cuda"))
+    assert torch.isnan(q.grad).any() and torch.isnan(d.grad).any()
+
+
+def test_golden_backward(fms):
+    from pathlib import Path
+    g = np.load(Path(__file__).parent / "golden" / "backward_small.npz")
+    Q, D = torch.from_numpy(g["Q"]).cuda(), torch.from_numpy(g["D"]).cuda()
+    qm = torch.from_numpy(g["qmask"]).cuda()
+    args = torch.from_numpy(g["args"]).cuda()
+    Dl = torch.from_numpy(g["Delta"]).cuda()
+    for code, sfx in ((0, "atomic"), (1, "invgrid")):
+        dQ, dD = fms.paired_pullback(Dl, Q, D, qm, args, None, strategy(fms, code))
+        close(dQ, g[f"dQ_{sfx}"], 1e-5, "golden dQ")
+        close(dD, g[f"dD_{sfx}"], 1e-5, "golden dD")
