@@ -36,6 +36,7 @@ _sz = C.c_size_t
 SIGNATURES = {
     "fms_status_string": (C.c_char_p, [_i]),
     "fms_version": (_i, []),
+    "fms_device_error": (_i, [_i]),
     "fms_pair_fwd": (_i, [_i, _P, _P, _P, _P, _i, _i, _i, _i, _P, _P, _P]),
     "fms_paired_fwd": (_i, [_i, _P, _P, _P, _P, _i, _i, _i, _i, _i, _P, _P, _P]),
     "fms_inbatch_fwd": (_i, [_i, _P, _P, _P, _P, _i, _i, _i, _i, _i, _i, _P, _P, _P]),

@@ -94,6 +94,8 @@ const char* fms_status_string(int status) {
 
 int fms_version(void) { return 100; }
 
+int fms_device_error(int reset) { return read_device_error(reset); }
+
 int fms_pair_fwd(int dtype, const void* q, const void* d, const uint8_t* qmask,
                  const uint8_t* dmask, int dim, int Tq, int Td, int normalize, void* score,
                  int32_t* args, fms_stream_t stream) {

@@ -21,6 +21,8 @@ cudaError_t launch_scan_simt(int dtype, const ScanParams& p, cudaStream_t s);
 // the SIMT scan, which is also a GPU kernel).
 cudaError_t launch_scan_tc(int dtype, const ScanParams& p, cudaStream_t s);
 bool scan_tc_supported(int dtype, const ScanParams& p);
+// Device health flag set by engine waits that timed out (0 = healthy).
+int read_device_error(int reset);
 
 cudaError_t launch_inv_counts(int dtype, const uint8_t* qmask, int Tq, int B, void* inv_n,
                               cudaStream_t s);

@@ -1,13 +1,537 @@
-// fms_scan_tc.cu -- tcgen05 + TMA MaxSim engine for 16-bit features (placeholder
-// until the engine lands: reports "not supported" so run_scan uses the CUDA-core
-// scan, which is also a GPU kernel).
+// fms_scan_tc.cu -- the sm_100a MaxSim engine for Float16 / BFloat16 features:
+// TMA-staged tiles, tcgen05 MMAs accumulating in TMEM, and the fused
+// max / argmax / Sigma_t epilogue read straight out of TMEM (the similarity
+// matrix never reaches HBM).  Replaces the reference's WMMA m16n16k16 scans
+// (ext/FlashMaxSimCUDAExt.jl:236-617) and its KA SRAM-tiled scans
+// (kernels_forward.jl:125-356, kernels_packed.jl:35-227) for 16-bit inputs.
+//
+// Orientation: query tokens on the MMA M side (64 or 128 rows per tile, up to
+// MAXMT tiles), document tokens on N (chunks of NT).  Each epilogue thread owns
+// one query-token row of the accumulator, so the per-token max over document
+// tokens is a register loop over TMEM columns -- no cross-thread reduction.
+//
+// Persistent CTAs walk the units (one query run x one document run); a unit may
+// stack several queries (in-batch, multi-query packed) so one document tile
+// feeds all of them.  Warp roles (192 threads):
+//   warp 0  TMA producer: per (chunk, 64-wide K block) loads the query tile(s)
+//           and the document rows of the chunk (64- and 16-row boxes, so padding
+//           beyond the last valid token of a document is not read) into a
+//           S-stage shared-memory ring;
+//   warp 1  MMA issuer (one elected lane): 4 K=16 MMAs per K block into one of
+//           two TMEM accumulator buffers, then tcgen05.commit to the ring slot
+//           and, after the chunk's last K block, to the accumulator barrier;
+//   warps 2-5  epilogue: tcgen05.ld 32 columns at a time, masked running
+//           (max, argmax) per row, then Sigma_t per query in t order, the
+//           normalisation and the `neg` fill; outputs written once.
+// Every wait is bounded: on a timeout the CTA raises an error flag, stops
+// issuing, lets in-flight copies land, frees TMEM and returns.
+#include <cuda.h>
+#include <mutex>
+
 #include "fms_common.cuh"
 #include "fms_internal.h"
+#include "fms_tc_ptx.cuh"
 
 namespace fms {
 
-bool scan_tc_supported(int, const ScanParams&) { return false; }
+__device__ int g_tc_error = 0;  // set when an engine wait timed out (diagnostic)
 
-cudaError_t launch_scan_tc(int, const ScanParams&, cudaStream_t) { return cudaErrorNotSupported; }
+namespace tc {
+
+constexpr int KBLK = 64;        // K elements per block: one 128-byte swizzled row
+constexpr int ROWB = 128;       // bytes per tile row
+constexpr int NTHREADS = 192;
+
+struct TcParams {
+  ScanParams p;
+  int G;          // queries stacked per unit (in-batch / packed), else 1
+  int ngroups;    // query groups
+  int64_t nunits;
+  int KB;         // K blocks (dim / 64)
+  uint32_t fmt;   // 0 = f16, 1 = bf16
+};
+
+struct TcUnit {
+  bool valid;
+  int64_t q_row0;
+  int nq;                 // queries in the unit
+  int Tq;                 // tokens per query
+  const uint8_t* qmask;   // mask of the unit's first query (stride Tq)
+  int64_t d_row0;
+  int Td;
+  const uint8_t* dmask;
+  int64_t out0, out_stride;
+  int64_t arg0, arg_stride;
+  int arg_rows;
+};
+
+__device__ __forceinline__ TcUnit tc_decode(const TcParams& P, int64_t v) {
+  const ScanParams& p = P.p;
+  TcUnit U;
+  if (p.layout == L_INBATCH || p.layout == L_PACKED) {
+    const int g = (int)(v % P.ngroups);
+    const int64_t j = v / P.ngroups;  // document: in-batch j, packed b
+    const int qi0 = g * P.G;
+    const int nqt = (p.layout == L_INBATCH) ? p.Bq : p.nq;
+    U.valid = true;
+    U.nq = min(P.G, nqt - qi0);
+    U.Tq = p.Tq;
+    U.q_row0 = (int64_t)qi0 * p.Tq;
+    U.qmask = p.qmask ? p.qmask + (int64_t)qi0 * p.Tq : nullptr;
+    U.arg_rows = p.Tq;
+    if (p.layout == L_INBATCH) {
+      U.d_row0 = j * p.Td;
+      U.Td = p.Td;
+      U.dmask = p.dmask ? p.dmask + j * p.Td : nullptr;
+      U.out0 = j + (int64_t)p.Bd * qi0;
+      U.out_stride = p.Bd;
+    } else {
+      U.d_row0 = (int64_t)p.cu_d[j] - 1;
+      U.Td = p.cu_d[j + 1] - p.cu_d[j];
+      clamp_run(U.d_row0, U.Td, p.nd_tok);
+      U.dmask = nullptr;
+      U.out0 = j + (int64_t)p.B * qi0;
+      U.out_stride = p.B;
+    }
+    U.arg0 = U.out0 * p.Tq;
+    U.arg_stride = U.out_stride * p.Tq;
+  } else {
+    const Unit u1 = decode_unit(p, v);
+    U.valid = u1.valid;
+    U.q_row0 = u1.q0;
+    U.nq = 1;
+    U.Tq = u1.Tq;
+    U.qmask = u1.qmask;
+    U.d_row0 = u1.d0;
+    U.Td = u1.Td;
+    U.dmask = u1.dmask;
+    U.out0 = u1.out;
+    U.out_stride = 0;
+    U.arg0 = u1.arg0;
+    U.arg_stride = 0;
+    U.arg_rows = u1.arg_rows;
+  }
+  return U;
+}
+
+// First valid document token and one past the last (warp-collective; every lane
+// gets the result).  Chunks stop at the last valid token, so masked padding at
+// the end of a document is never read from HBM.
+__device__ __forceinline__ void doc_extent(const uint8_t* dmask, int Td, int& first, int& leff) {
+  if (dmask == nullptr) {
+    first = Td > 0 ? 0 : -1;
+    leff = Td;
+    return;
+  }
+  const int lane = threadIdx.x & 31;
+  int f = -1, l = -1;
+  for (int u0 = 0; u0 < Td; u0 += 32) {
+    const int u = u0 + lane;
+    const bool ok = u < Td && dmask[u] != 0;
+    const unsigned b = __ballot_sync(0xffffffffu, ok);
+    if (b) {
+      if (f < 0) f = u0 + __ffs(b) - 1;
+      l = u0 + 31 - __clz(b);
+    }
+  }
+  first = f;
+  leff = l + 1;
+}
+
+template <int M, int NT, int MAXMT, int S>
+struct Smem {
+  static constexpr int A_BYTES = MAXMT * M * ROWB;   // one K block of all M tiles
+  static constexpr int B_BYTES = NT * ROWB;          // one K block of the chunk
+  static constexpr int STAGE = A_BYTES + B_BYTES;
+  static constexpr int TILES = S * STAGE;
+  static constexpr int ACC_COLS = MAXMT * NT;        // TMEM columns per accumulator buffer
+  static constexpr int TMEM_COLS = 2 * ACC_COLS;     // double-buffered
+  static constexpr int DYN = TILES + 1024;           // + alignment slack
+};
+
+template <int M, int NT, int MAXMT, int S, bool ARGS>
+__global__ void __launch_bounds__(NTHREADS, 1)
+tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB64,
+               const __grid_constant__ CUtensorMap tmB16, TcParams P) {
+  using L = Smem<M, NT, MAXMT, S>;
+  static_assert(L::TMEM_COLS == 128 || L::TMEM_COLS == 256 || L::TMEM_COLS == 512, "TMEM cols");
+  extern __shared__ __align__(1024) unsigned char dsm[];
+  __shared__ __align__(8) uint64_t full_bar[S];
+  __shared__ __align__(8) uint64_t empty_bar[S];
+  __shared__ __align__(8) uint64_t accf_bar[2];
+  __shared__ __align__(8) uint64_t acce_bar[2];
+  __shared__ __align__(8) uint64_t epi_bar;  // epilogue-wide barrier (bounded, unlike bar.sync)
+  __shared__ uint32_t tmem_base_s;
+  __shared__ volatile int abort_s;
+  __shared__ float red_s[MAXMT * M];
+
+  unsigned char* tiles = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(dsm) + 1023) & ~(uintptr_t)1023);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const ScanParams& p = P.p;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      ptx::mbar_init(&full_bar[i], 1);
+      ptx::mbar_init(&empty_bar[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      ptx::mbar_init(&accf_bar[i], 1);
+      ptx::mbar_init(&acce_bar[i], 4);  // one arrival per epilogue warp
+    }
+    ptx::mbar_init(&epi_bar, 128);
+    abort_s = 0;
+    ptx::fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    ptx::prefetch_tmap(&tmA);
+    ptx::prefetch_tmap(&tmB64);
+    ptx::prefetch_tmap(&tmB16);
+  }
+  if (warp == 1) ptx::tmem_alloc(&tmem_base_s, L::TMEM_COLS);
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = tmem_base_s;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int64_t v = blockIdx.x; v < P.nunits && !abort_s; v += gridDim.x) {
+      const TcUnit U = tc_decode(P, v);
+      if (!U.valid) continue;
+      int first, leff;
+      doc_extent(U.dmask, U.Td, first, leff);
+      const int rows = U.nq * U.Tq;
+      if (rows == 0) continue;
+      const int nmt = (rows + M - 1) / M;
+      const int nch = (leff + NT - 1) / NT;
+      for (int c = 0; c < nch; ++c) {
+        const int u0 = c * NT;
+        const int n = min(NT, leff - u0);
+        const int nr = (n + 15) & ~15;
+        for (int kb = 0; kb < P.KB; ++kb) {
+          if (!ptx::mbar_wait(&empty_bar[stage], phase ^ 1, &abort_s)) goto done;
+          if (lane == 0) {
+            unsigned char* sA = tiles + stage * L::STAGE;
+            unsigned char* sB = sA + L::A_BYTES;
+            ptx::mbar_expect_tx(&full_bar[stage], (uint32_t)(nmt * M * ROWB + nr * ROWB));
+            for (int mt = 0; mt < nmt; ++mt)
+              ptx::tma_load_2d(sA + mt * M * ROWB, &tmA, kb * KBLK, (int)(U.q_row0 + mt * M),
+                               &full_bar[stage]);
+            int r = 0;
+            for (; r + 64 <= nr; r += 64)
+              ptx::tma_load_2d(sB + r * ROWB, &tmB64, kb * KBLK, (int)(U.d_row0 + u0 + r),
+                               &full_bar[stage]);
+            for (; r < nr; r += 16)
+              ptx::tma_load_2d(sB + r * ROWB, &tmB16, kb * KBLK, (int)(U.d_row0 + u0 + r),
+                               &full_bar[stage]);
+          }
+          __syncwarp();
+          if (++stage == S) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    int stage = 0;
+    uint32_t phase = 0;
+    int as = 0;
+    uint32_t aphase = 0;
+    for (int64_t v = blockIdx.x; v < P.nunits && !abort_s; v += gridDim.x) {
+      const TcUnit U = tc_decode(P, v);
+      if (!U.valid) continue;
+      int first, leff;
+      doc_extent(U.dmask, U.Td, first, leff);
+      const int rows = U.nq * U.Tq;
+      if (rows == 0) continue;
+      const int nmt = (rows + M - 1) / M;
+      const int nch = (leff + NT - 1) / NT;
+      for (int c = 0; c < nch; ++c) {
+        const int n = min(NT, leff - c * NT);
+        const int nr = (n + 15) & ~15;
+        const uint32_t idesc = ptx::idesc_f16(P.fmt, M, nr);
+        if (!ptx::mbar_wait(&acce_bar[as], aphase ^ 1, &abort_s)) goto done;
+        ptx::tc_fence_after();
+        for (int kb = 0; kb < P.KB; ++kb) {
+          if (!ptx::mbar_wait(&full_bar[stage], phase, &abort_s)) goto done;
+          ptx::tc_fence_after();
+          if (lane == 0) {
+            const uint32_t sA = ptx::smem_u32(tiles + stage * L::STAGE);
+            const uint32_t sB = sA + L::A_BYTES;
+            const uint64_t bdesc = ptx::sw128_desc(sB);
+            for (int mt = 0; mt < nmt; ++mt) {
+              const uint64_t adesc = ptx::sw128_desc(sA + mt * M * ROWB);
+              const uint32_t d = tmem_base + (uint32_t)(as * L::ACC_COLS + mt * NT);
+#pragma unroll
+              for (int k = 0; k < KBLK / 16; ++k)
+                ptx::mma_f16(d, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0);
+            }
+            ptx::mma_commit(&empty_bar[stage]);
+          }
+          __syncwarp();
+          if (++stage == S) { stage = 0; phase ^= 1; }
+        }
+        if (lane == 0) ptx::mma_commit(&accf_bar[as]);
+        __syncwarp();
+        as ^= 1;
+        if (as == 0) aphase ^= 1;
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    using A = float;
+    const int sp = warp & 3;                       // TMEM subpartition of this warp
+    const int et = threadIdx.x - 64;               // 0..127
+    const int lr = (M == 128) ? sp * 32 + lane : (lane < 16 ? sp * 16 + lane : -1);
+    int as = 0;
+    uint32_t aphase = 0;
+    uint32_t ephase = 0;
+    float* scores = static_cast<float*>(p.scores);
+    for (int64_t v = blockIdx.x; v < P.nunits; v += gridDim.x) {
+      if (abort_s) break;
+      const TcUnit U = tc_decode(P, v);
+      if (!U.valid) {
+        if (et == 0) scores[U.out0] = (float)p.neg;
+        if (ARGS)
+          for (int t = et; t < U.arg_rows; t += 128) p.args[U.arg0 + t] = 0;
+        continue;
+      }
+      int first, leff;
+      doc_extent(U.dmask, U.Td, first, leff);
+      const int rows = U.nq * U.Tq;
+      const int nmt = (rows + M - 1) / M;
+      const int nch = rows == 0 ? 0 : (leff + NT - 1) / NT;
+      A mx[MAXMT], s0[MAXMT];
+      int ag[MAXMT];
+#pragma unroll
+      for (int mt = 0; mt < MAXMT; ++mt) { mx[mt] = -INFINITY; ag[mt] = 0; s0[mt] = 0.f; }
+      for (int c = 0; c < nch; ++c) {
+        const int u0 = c * NT;
+        const int n = min(NT, leff - u0);
+        uint32_t mw[NT / 32];
+#pragma unroll
+        for (int g = 0; g < NT / 32; ++g) {
+          const int cc = 32 * g + lane;
+          const bool ok = cc < n && (U.dmask == nullptr || U.dmask[u0 + cc] != 0);
+          mw[g] = __ballot_sync(0xffffffffu, ok);
+        }
+        if (!ptx::mbar_wait(&accf_bar[as], aphase, &abort_s)) goto done;
+        ptx::tc_fence_after();
+        const uint32_t tb = tmem_base + ((uint32_t)(sp * 32) << 16) + (uint32_t)(as * L::ACC_COLS);
+#pragma unroll
+        for (int mt = 0; mt < MAXMT; ++mt) {
+          if (mt < nmt) {
+#pragma unroll
+            for (int g = 0; g < NT / 32; ++g) {
+              if (32 * g < n) {
+                uint32_t r[32];
+                ptx::tmem_ld32(tb + mt * NT + 32 * g, r);
+                ptx::tmem_wait_ld();
+                const uint32_t m = mw[g];
+#pragma unroll
+                for (int cc = 0; cc < 32; ++cc) {
+                  const A s = __uint_as_float(r[cc]);
+                  if (((m >> cc) & 1u) && s > mx[mt]) {
+                    mx[mt] = s;
+                    ag[mt] = u0 + 32 * g + cc + 1;
+                  }
+                }
+              }
+            }
+            if (first >= u0 && first < u0 + NT) {
+              s0[mt] = __uint_as_float(ptx::tmem_ld1(tb + mt * NT + (first - u0)));
+              ptx::tmem_wait_ld();
+            }
+          }
+        }
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&acce_bar[as]);
+        as ^= 1;
+        if (as == 0) aphase ^= 1;
+      }
+      // finish the rows: exact first-valid rule, tape, per-row contribution
+#pragma unroll
+      for (int mt = 0; mt < MAXMT; ++mt) {
+        const int r = mt * M + lr;
+        if (mt < nmt && lr >= 0 && r < rows) {
+          const int qi = r / U.Tq, t = r - qi * U.Tq;
+          const bool tv = U.qmask == nullptr || U.qmask[r] != 0;
+          A m = mx[mt];
+          int a = ag[mt];
+          final_fixup(m, a, first, s0[mt]);
+          const bool ok = tv && a > 0;
+          red_s[r] = ok ? m : 0.f;
+          if (ARGS) p.args[U.arg0 + qi * U.arg_stride + t] = ok ? a : 0;
+        }
+      }
+      ptx::mbar_arrive(&epi_bar);
+      if (!ptx::mbar_wait(&epi_bar, ephase, &abort_s)) goto done;
+      ephase ^= 1;
+      if (et < U.nq) {
+        const int qi = et;
+        A score = 0.f;
+        int nvalid = 0;
+        for (int t = 0; t < U.Tq; ++t) {
+          score += red_s[qi * U.Tq + t];
+          nvalid += (U.qmask == nullptr || U.qmask[qi * U.Tq + t]) ? 1 : 0;
+        }
+        if (p.normalize) score = score * (1.0f / (float)(nvalid > 1 ? nvalid : 1));
+        scores[U.out0 + qi * U.out_stride] = score;
+      }
+      if (ARGS)
+        for (int t = U.Tq + et; t < U.arg_rows; t += 128) p.args[U.arg0 + t] = 0;
+      ptx::mbar_arrive(&epi_bar);  // red_s is reused by the next unit
+      if (!ptx::mbar_wait(&epi_bar, ephase, &abort_s)) goto done;
+      ephase ^= 1;
+    }
+  }
+done:
+  if (abort_s && threadIdx.x == 0) {
+    atomicExch(&g_tc_error, 1);
+    // let copies and MMAs already in flight land before shared memory and TMEM go away
+    const uint64_t t0 = ptx::globaltimer_ns();
+    while (ptx::globaltimer_ns() - t0 < 50000ull) {
+    }
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem_base, L::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------- host side
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+// 2-D map over a token matrix (dim, rows) of 16-bit elements: box 64 x box_rows,
+// 128-byte swizzle, zero fill out of bounds.
+static bool make_map(CUtensorMap* m, const void* base, uint32_t fmt, int dim, int64_t rows, int box_rows) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t gdim[2] = {(cuuint64_t)dim, (cuuint64_t)rows};
+  cuuint64_t gstride[1] = {(cuuint64_t)dim * 2};
+  cuuint32_t box[2] = {(cuuint32_t)KBLK, (cuuint32_t)box_rows};
+  cuuint32_t estride[2] = {1, 1};
+  CUresult r = enc(m, fmt == 0 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                   const_cast<void*>(base), gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+static int queries_total(const ScanParams& p) {
+  return p.layout == L_INBATCH ? p.Bq : (p.layout == L_PACKED ? p.nq : 1);
+}
+
+// Queries stacked per unit and the resulting row count.
+static void plan(const ScanParams& p, int& G, int& rows) {
+  const int Tq = p.Tq;
+  G = 1;
+  if ((p.layout == L_INBATCH || p.layout == L_PACKED) && Tq > 0) {
+    G = 256 / Tq;
+    if (G < 1) G = 1;
+    const int nq = queries_total(p);
+    if (G > nq) G = nq > 0 ? nq : 1;
+  }
+  rows = G * Tq;
+}
+
+template <int M, int NT, int MAXMT, int S>
+static cudaError_t launch_cfg(const TcParams& P, const CUtensorMap& a, const CUtensorMap& b64,
+                              const CUtensorMap& b16, cudaStream_t s, int ctas_per_sm) {
+  using L = Smem<M, NT, MAXMT, S>;
+  int64_t grid = (int64_t)device_sm_count() * ctas_per_sm;
+  if (grid > P.nunits) grid = P.nunits;
+  if (grid < 1) grid = 1;
+  cudaError_t e;
+  if (P.p.args) {
+    auto k = tc_scan_kernel<M, NT, MAXMT, S, true>;
+    if ((e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, L::DYN)) != cudaSuccess)
+      return e;
+    k<<<(unsigned)grid, NTHREADS, L::DYN, s>>>(a, b64, b16, P);
+  } else {
+    auto k = tc_scan_kernel<M, NT, MAXMT, S, false>;
+    if ((e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, L::DYN)) != cudaSuccess)
+      return e;
+    k<<<(unsigned)grid, NTHREADS, L::DYN, s>>>(a, b64, b16, P);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace tc
+
+int read_device_error(int reset) {
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_tc_error, sizeof(int));
+  if (e != cudaSuccess) return (int)e;
+  if (reset) {
+    int z = 0;
+    e = cudaMemcpyToSymbol(g_tc_error, &z, sizeof(int));
+    if (e != cudaSuccess) return (int)e;
+  }
+  return v;
+}
+
+bool scan_tc_supported(int dtype, const ScanParams& p) {
+  if (dtype != FMS_F16 && dtype != FMS_BF16) return false;
+  if (device_cc() != 100) return false;
+  if (tc::encode_fn() == nullptr) return false;
+  if (p.dim <= 0 || p.dim % tc::KBLK != 0) return false;
+  if (p.nq_tok <= 0 || p.nd_tok <= 0 || p.nq_tok >= INT32_MAX || p.nd_tok >= INT32_MAX) return false;
+  if ((reinterpret_cast<uintptr_t>(p.Q) & 15) || (reinterpret_cast<uintptr_t>(p.D) & 15)) return false;
+  if (p.Tq <= 0) return false;
+  int G, rows;
+  tc::plan(p, G, rows);
+  return rows <= 256;
+}
+
+cudaError_t launch_scan_tc(int dtype, const ScanParams& p, cudaStream_t s) {
+  if (!scan_tc_supported(dtype, p)) return cudaErrorNotSupported;
+  tc::TcParams P;
+  P.p = p;
+  int G, rows;
+  tc::plan(p, G, rows);
+  P.G = G;
+  const int nqt = tc::queries_total(p);
+  P.ngroups = (p.layout == L_INBATCH || p.layout == L_PACKED) ? (nqt + G - 1) / G : 1;
+  if (p.layout == L_INBATCH)
+    P.nunits = (int64_t)p.Bd * P.ngroups;
+  else if (p.layout == L_PACKED)
+    P.nunits = (int64_t)p.B * P.ngroups;
+  else
+    P.nunits = p.nunits;
+  P.KB = p.dim / tc::KBLK;
+  P.fmt = dtype == FMS_BF16 ? 1u : 0u;
+  if (P.nunits == 0) return cudaSuccess;
+  const int M = rows <= 64 ? 64 : 128;
+  CUtensorMap a, b64, b16;
+  if (!tc::make_map(&a, p.Q, P.fmt, p.dim, p.nq_tok, M)) return cudaErrorNotSupported;
+  if (!tc::make_map(&b64, p.D, P.fmt, p.dim, p.nd_tok, 64)) return cudaErrorNotSupported;
+  if (!tc::make_map(&b16, p.D, P.fmt, p.dim, p.nd_tok, 16)) return cudaErrorNotSupported;
+  if (rows <= 64) return tc::launch_cfg<64, 128, 1, 4>(P, a, b64, b16, s, 2);
+  if (rows <= 128) return tc::launch_cfg<128, 128, 1, 3>(P, a, b64, b16, s, 2);
+  return tc::launch_cfg<128, 128, 2, 4>(P, a, b64, b16, s, 1);
+}
 
 }  // namespace fms

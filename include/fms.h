@@ -57,6 +57,13 @@ const char* fms_status_string(int status);
 /* Library ABI version: major*10000 + minor*100 + patch. */
 int fms_version(void);
 
+/* Device-side health flag of the current device: 1 if a kernel's bounded wait
+   timed out since the last reset (that launch stopped early and its outputs are
+   invalid), else 0; negative / positive status codes on failure.  Synchronizes
+   the device.  reset != 0 clears the flag.  (No reference counterpart: the
+   reference's kernels have no device-side waits.) */
+int fms_device_error(int reset);
+
 /* ------------------------------------------------------------------ forward */
 
 /* Pair: score (1,) = maxsim(q, d, qmask, dmask), args (Tq,).

@@ -40,11 +40,11 @@ def lib():
     global _lib
     if _lib is not None:
         return _lib
-    import sys
-    sys.path.insert(0, str(_HERE))
-    from build import build  # oracle/build.py
-    sys.path.pop(0)
-    path = build()
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("fms_oracle_build", _HERE / "build.py")
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    path = mod.build()
     L = C.CDLL(str(path))
     i, i64, f, d = C.c_int, C.c_int64, C.c_float, C.c_double
     for suf, AP, A in (("f32", F32P, f), ("f64", F64P, d)):

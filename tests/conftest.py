@@ -36,6 +36,17 @@ def pytest_collection_modifyitems(config, items):
             it.add_marker(skip)
 
 
+@pytest.fixture(autouse=True)
+def _device_health(request):
+    """After every GPU test: no kernel wait of the engine may have timed out."""
+    yield
+    if "gpu" in request.keywords:
+        import torch
+        if torch.cuda.is_available():
+            import flashmaxsim_b200 as F
+            assert F.load_library().fms_device_error(1) == 0, "an engine wait timed out"
+
+
 @pytest.fixture(scope="session")
 def oracle():
     import oracle as O  # oracle/oracle.py

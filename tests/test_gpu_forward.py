@@ -93,9 +93,11 @@ def test_candidates(fms, oracle, dt):
     lens = rng.integers(8, Td + 1, N)
     dm = torch.from_numpy(np.arange(Td)[None, :] < lens[:, None]).cuda()
     ix = torch.from_numpy(idxs).cuda()
-    for neg in (-1.0e4, float("-inf")):
+    for neg0 in (-1.0e4, float("-inf")):
+        # MaxSim{T} stores T(neg) (types.jl:34-37): bf16 rounds -1e4 to -9984
+        neg = float(torch.tensor(neg0, dtype=dtype).item())
         for norm in (False, True):
-            S, A = fms.candidates_forward(Q, G, ix, None, dm, neg=neg, normalize=norm)
+            S, A = fms.candidates_forward(Q, G, ix, None, dm, neg=neg0, normalize=norm)
             So, Ao = oracle.candidates(Q, G, idxs, None, dm.cpu(), neg=neg, normalize=norm)
             assert_scores(S.cpu(), So, tol)
             assert S[0, 3].item() == neg and S[2, 1].item() == neg and S[3, 6].item() == neg

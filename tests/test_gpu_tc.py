@@ -1,0 +1,91 @@
+"""Parity of the tcgen05 + TMA engine (16-bit features, dim a multiple of 64) at
+shapes of the benchmark configs, scaled down so the oracle finishes in seconds:
+candidates (Tq 32, Td 256, prefix masks, 2% invalid), in-batch (dim 768, split-d
+K loop), multi-query packed (16 queries x 24 tokens) and paired."""
+import numpy as np
+import pytest
+import torch
+
+from conftest import assert_args, assert_scores, seeded
+
+pytestmark = pytest.mark.gpu
+
+
+def l2t(x):
+    return x / x.norm(dim=-1, keepdim=True)
+
+
+def sims(q, d):
+    return q.double().cpu().numpy() @ d.double().cpu().numpy().T
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("args_on", [True, False])
+def test_candidates_c2_like(fms, oracle, dtype, args_on):
+    g = torch.Generator().manual_seed(2)
+    B, C, Tq, Td, N, dim = 6, 300, 32, 256, 700, 128
+    Q = l2t(torch.randn(B, Tq, dim, generator=g)).to(dtype).cuda()
+    G = l2t(torch.randn(N, Td, dim, generator=g)).to(dtype).cuda()
+    lens = torch.randint(64, Td + 1, (N,), generator=g)
+    dm = (torch.arange(Td)[None, :] < lens[:, None])
+    idxs = torch.randint(1, N + 1, (B, C), generator=g, dtype=torch.int32)
+    idxs[torch.rand(B, C, generator=g) < 0.02] = 0
+    S, A = fms.candidates_forward(Q, G, idxs.cuda(), None, dm.cuda(), neg=float("-inf"),
+                                  want_args=args_on)
+    So, Ao = oracle.candidates(Q, G, idxs, None, dm, neg=float("-inf"))
+    assert_scores(S.cpu(), So, 1e-3)
+    if args_on:
+        Gc, Qc, ix = G.cpu(), Q.cpu(), idxs.numpy()
+        assert_args(A.cpu(), Ao, lambda i, u: sims(Qc[i[0]], Gc[ix[i[0], i[1]] - 1])[i[2], u - 1],
+                    1e-3)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_inbatch_c3_like(fms, oracle, dtype):
+    g = torch.Generator().manual_seed(3)
+    Bq, Bd, Tq, Td, dim = 12, 10, 32, 180, 768
+    Q = l2t(torch.randn(Bq, Tq, dim, generator=g)).to(dtype).cuda()
+    D = l2t(torch.randn(Bd, Td, dim, generator=g)).to(dtype).cuda()
+    lens = torch.randint(32, Td + 1, (Bd,), generator=g)
+    dm = (torch.arange(Td)[None, :] < lens[:, None])
+    qm = torch.rand(Bq, Tq, generator=g) > 0.1
+    for norm in (False, True):
+        S, A = fms.inbatch_forward(Q, D, qm.cuda(), dm.cuda(), normalize=norm)
+        So, Ao = oracle.inbatch(Q, D, qm, dm, normalize=norm)
+        assert_scores(S.cpu(), So, 1e-3)
+        Qc, Dc = Q.cpu(), D.cpu()
+        assert_args(A.cpu(), Ao, lambda i, u: sims(Qc[i[0]], Dc[i[1]])[i[2], u - 1], 1e-3)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_packed_c4_like(fms, oracle, dtype):
+    g = torch.Generator().manual_seed(4)
+    nq, Tq, dim = 16, 24, 128
+    lens = torch.randint(700, 1031, (40,), generator=g).tolist()
+    lens[3] = 0
+    docs = [l2t(torch.randn(n, dim, generator=g)).to(dtype).cuda() for n in lens]
+    P = fms.pack_docs(docs)
+    Qs = l2t(torch.randn(nq, Tq, dim, generator=g)).to(dtype).cuda()
+    S, A = fms.packed_forward(Qs, P)
+    So, Ao = oracle.packed(Qs, P.tokens, P.cu.cpu())
+    assert_scores(S.cpu(), So, 1e-3)
+    assert S[:, 3].abs().max().item() == 0
+    Qc, tok, cu = Qs.cpu(), P.tokens.cpu(), P.cu.cpu().numpy()
+    assert_args(A.cpu(), Ao,
+                lambda i, u: sims(Qc[i[0]], tok[cu[i[1]] - 1:cu[i[1] + 1] - 1])[i[2], u - 1], 1e-3)
+
+
+@pytest.mark.parametrize("Tq,Td", [(32, 180), (64, 300), (100, 129), (200, 77), (7, 1000)])
+def test_paired_row_configs(fms, oracle, Tq, Td):
+    """Every engine configuration: 64-row, 128-row and 2 x 128-row query tiles."""
+    g = torch.Generator().manual_seed(Tq + Td)
+    B, dim = 5, 128
+    Q = l2t(torch.randn(B, Tq, dim, generator=g)).half().cuda()
+    D = l2t(torch.randn(B, Td, dim, generator=g)).half().cuda()
+    qm = torch.rand(B, Tq, generator=g) > 0.2
+    dm = torch.rand(B, Td, generator=g) > 0.3
+    s, a = fms.paired_forward(Q, D, qm.cuda(), dm.cuda())
+    so, ao = oracle.paired(Q, D, qm, dm)
+    assert_scores(s.cpu(), so, 1e-3)
+    Qc, Dc = Q.cpu(), D.cpu()
+    assert_args(a.cpu(), ao, lambda i, u: sims(Qc[i[0]], Dc[i[0]])[i[1], u - 1], 1e-3)
