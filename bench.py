@@ -47,6 +47,10 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    # smaller galleries for ncu captures (a few GB on the device); the bench
+    # line itself always uses the defaults
+    ap.add_argument("--ndoc", type=int, default=NDOC)
+    ap.add_argument("--ncand", type=int, default=C)
     return ap.parse_args()
 
 
@@ -228,7 +232,9 @@ def run_reference(args, world, rank):
 
 
 def main():
+    global NDOC, C
     args = parse()
+    NDOC, C = args.ndoc, args.ncand
     world, rank, local = dist_setup(args)
     if args.impl == "reference":
         run_reference(args, world, rank)

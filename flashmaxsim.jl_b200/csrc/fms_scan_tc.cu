@@ -124,17 +124,49 @@ __device__ __forceinline__ void doc_extent(const uint8_t* dmask, int Td, int& fi
     return;
   }
   const int lane = threadIdx.x & 31;
-  int f = -1, l = -1;
-  for (int u0 = 0; u0 < Td; u0 += 32) {
-    const int u = u0 + lane;
-    const bool ok = u < Td && dmask[u] != 0;
-    const unsigned b = __ballot_sync(0xffffffffu, ok);
-    if (b) {
-      if (f < 0) f = u0 + __ffs(b) - 1;
-      l = u0 + 31 - __clz(b);
+  int f = INT32_MAX, l = -1;
+  if ((reinterpret_cast<uintptr_t>(dmask) & 15) == 0) {
+    // 16 mask bytes per lane per load: one round trip covers 512 tokens
+    for (int u0 = 0; u0 < Td; u0 += 512) {
+      const int base = u0 + lane * 16;
+      uint32_t w[4] = {0u, 0u, 0u, 0u};
+      if (base + 16 <= Td) {
+        const uint4 x = *reinterpret_cast<const uint4*>(dmask + base);
+        w[0] = x.x; w[1] = x.y; w[2] = x.z; w[3] = x.w;
+      } else {
+        for (int i = 0; i < 16 && base + i < Td; ++i) w[i >> 2] |= (uint32_t)dmask[base + i] << (8 * (i & 3));
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        if ((w[i >> 2] >> (8 * (i & 3))) & 0xffu) {
+          f = min(f, base + i);
+          l = max(l, base + i);
+        }
+      }
+    }
+  } else {
+    for (int u0 = 0; u0 < Td; u0 += 128) {
+      uint8_t b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int u = u0 + i * 32 + lane;
+        b[i] = u < Td ? dmask[u] : 0;
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        if (b[i]) {
+          const int u = u0 + i * 32 + lane;
+          f = min(f, u);
+          l = max(l, u);
+        }
     }
   }
-  first = f;
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    f = min(f, __shfl_xor_sync(0xffffffffu, f, off));
+    l = max(l, __shfl_xor_sync(0xffffffffu, l, off));
+  }
+  first = f == INT32_MAX ? -1 : f;
   leff = l + 1;
 }
 
@@ -164,6 +196,7 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   __shared__ uint32_t tmem_base_s;
   __shared__ volatile int abort_s;
   __shared__ float red_s[MAXMT * M];
+  __shared__ uint8_t tv_s[MAXMT * M];
 
   unsigned char* tiles = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(dsm) + 1023) & ~(uintptr_t)1023);
@@ -365,6 +398,7 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           final_fixup(m, a, first, s0[mt]);
           const bool ok = tv && a > 0;
           red_s[r] = ok ? m : 0.f;
+          tv_s[r] = tv ? 1 : 0;
           if (ARGS) p.args[U.arg0 + qi * U.arg_stride + t] = ok ? a : 0;
         }
       }
@@ -375,9 +409,10 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const int qi = et;
         A score = 0.f;
         int nvalid = 0;
-        for (int t = 0; t < U.Tq; ++t) {
+#pragma unroll 8
+        for (int t = 0; t < U.Tq; ++t) {  // Sigma_t in t order (forward_pair.jl:92-95)
           score += red_s[qi * U.Tq + t];
-          nvalid += (U.qmask == nullptr || U.qmask[qi * U.Tq + t]) ? 1 : 0;
+          nvalid += tv_s[qi * U.Tq + t];
         }
         if (p.normalize) score = score * (1.0f / (float)(nvalid > 1 ? nvalid : 1));
         scores[U.out0 + qi * U.out_stride] = score;
