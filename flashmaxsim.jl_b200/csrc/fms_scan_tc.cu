@@ -9,23 +9,31 @@
 // MAXMT tiles), document tokens on N (chunks of NT).  Each epilogue thread owns
 // one query-token row of the accumulator, so the per-token max over document
 // tokens is a register loop over TMEM columns -- no cross-thread reduction.
+// For queries of <= 32 tokens the 64-row tile holds the query twice (R = 2):
+// the MMA cost is the same, and the two copies let all four TMEM subpartitions
+// (all four epilogue warps) work, each on half of the chunk's columns.
 //
 // Persistent CTAs walk the units (one query run x one document run); a unit may
 // stack several queries (in-batch, multi-query packed) so one document tile
-// feeds all of them.  Warp roles (192 threads):
+// feeds all of them.  Warp roles (224 threads):
+//   warp 6  scheduler: decodes 32 upcoming units at once (one per lane: candidate
+//           index, CSR bounds, first / last valid document token, document and
+//           query mask bits) into a 16-entry shared-memory metadata ring, so the
+//           dependent index -> mask global loads are off the other roles' paths;
 //   warp 0  TMA producer: per (chunk, 64-wide K block) loads the query tile(s)
-//           and the document rows of the chunk (64- and 16-row boxes, so padding
-//           beyond the last valid token of a document is not read) into a
-//           S-stage shared-memory ring;
+//           and the document rows of the chunk (64- and 16-row boxes, stopping at
+//           the last valid token, so masked padding is not read) into an S-stage
+//           ring;
 //   warp 1  MMA issuer (one elected lane): 4 K=16 MMAs per K block into one of
-//           two TMEM accumulator buffers, then tcgen05.commit to the ring slot
-//           and, after the chunk's last K block, to the accumulator barrier;
+//           two TMEM accumulator buffers, tcgen05.commit to the ring slot and,
+//           after the chunk's last K block, to the accumulator barrier;
 //   warps 2-5  epilogue: tcgen05.ld 32 columns at a time, masked running
 //           (max, argmax) per row, then Sigma_t per query in t order, the
-//           normalisation and the `neg` fill; outputs written once.
+//           normalisation and the `neg` fill; every output written once.
 // Every wait is bounded: on a timeout the CTA raises an error flag, stops
 // issuing, lets in-flight copies land, frees TMEM and returns.
 #include <cuda.h>
+#include <stdlib.h>
 #include <mutex>
 
 #include "fms_common.cuh"
@@ -38,9 +46,14 @@ __device__ int g_tc_error = 0;  // set when an engine wait timed out (diagnostic
 
 namespace tc {
 
-constexpr int KBLK = 64;        // K elements per block: one 128-byte swizzled row
-constexpr int ROWB = 128;       // bytes per tile row
-constexpr int NTHREADS = 192;
+constexpr int KBLK = 64;    // K elements per block: one 128-byte swizzled row
+constexpr int ROWB = 128;   // bytes per tile row
+constexpr int NWARPS = 7;
+constexpr int NTHREADS = NWARPS * 32;
+constexpr int SCHED_WARP = 6;
+constexpr int UQ = 16;      // metadata ring depth (units)
+constexpr int MW_MAX = 16;  // document-mask words carried per unit (Td <= 512)
+constexpr int QW_MAX = 8;   // query-row valid words (rows <= 256)
 
 struct TcParams {
   ScanParams p;
@@ -63,6 +76,15 @@ struct TcUnit {
   int64_t out0, out_stride;
   int64_t arg0, arg_stride;
   int arg_rows;
+};
+
+// One unit as the other roles see it (written by the scheduler warp).
+struct UnitMeta {
+  int64_t q_row0, d_row0, out0, out_stride, arg0, arg_stride;
+  const uint8_t* dmask;   // kept for documents longer than 32*MW_MAX tokens
+  int nq, Tq, leff, first, valid, arg_rows, mw_ok, pad;
+  uint32_t mw[MW_MAX];    // bit u: document token u valid (u < 32*MW_MAX)
+  uint32_t qw[QW_MAX];    // bit r: query row r valid
 };
 
 __device__ __forceinline__ TcUnit tc_decode(const TcParams& P, int64_t v) {
@@ -114,89 +136,82 @@ __device__ __forceinline__ TcUnit tc_decode(const TcParams& P, int64_t v) {
   return U;
 }
 
-// First valid document token and one past the last (warp-collective; every lane
-// gets the result).  Chunks stop at the last valid token, so masked padding at
-// the end of a document is never read from HBM.
-__device__ __forceinline__ void doc_extent(const uint8_t* dmask, int Td, int& first, int& leff) {
-  if (dmask == nullptr) {
-    first = Td > 0 ? 0 : -1;
-    leff = Td;
+// Nonzero bytes of a 32-bit word -> 4 bits.
+__device__ __forceinline__ uint32_t nz4(uint32_t w) {
+  const uint32_t r = __vcmpne4(w, 0u);
+  return (r & 1u) | ((r >> 7) & 2u) | ((r >> 14) & 4u) | ((r >> 21) & 8u);
+}
+
+// Bits of n mask bytes (0/1) starting at m into words (per thread, sequential
+// loads; 16-byte vector loads when aligned).  Bits past n are zero.
+template <int W>
+__device__ __forceinline__ void mask_bits(const uint8_t* m, int n, uint32_t (&w)[W]) {
+#pragma unroll
+  for (int i = 0; i < W; ++i) w[i] = 0u;
+  if (m == nullptr) {
+#pragma unroll
+    for (int i = 0; i < W; ++i) {
+      const int lo = 32 * i;
+      w[i] = n >= lo + 32 ? 0xffffffffu : (n > lo ? ((1u << (n - lo)) - 1u) : 0u);
+    }
     return;
   }
-  const int lane = threadIdx.x & 31;
-  int f = INT32_MAX, l = -1;
-  if ((reinterpret_cast<uintptr_t>(dmask) & 15) == 0) {
-    // 16 mask bytes per lane per load: one round trip covers 512 tokens
-    for (int u0 = 0; u0 < Td; u0 += 512) {
-      const int base = u0 + lane * 16;
-      uint32_t w[4] = {0u, 0u, 0u, 0u};
-      if (base + 16 <= Td) {
-        const uint4 x = *reinterpret_cast<const uint4*>(dmask + base);
-        w[0] = x.x; w[1] = x.y; w[2] = x.z; w[3] = x.w;
-      } else {
-        for (int i = 0; i < 16 && base + i < Td; ++i) w[i >> 2] |= (uint32_t)dmask[base + i] << (8 * (i & 3));
-      }
+  if ((reinterpret_cast<uintptr_t>(m) & 15) == 0) {
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        if ((w[i >> 2] >> (8 * (i & 3))) & 0xffu) {
-          f = min(f, base + i);
-          l = max(l, base + i);
+    for (int i = 0; i < 2 * W; ++i) {  // 16 bytes per step
+      const int base = 16 * i;
+      if (base < n) {
+        uint32_t bits;
+        if (base + 16 <= n) {
+          const uint4 x = __ldg(reinterpret_cast<const uint4*>(m + base));
+          bits = nz4(x.x) | (nz4(x.y) << 4) | (nz4(x.z) << 8) | (nz4(x.w) << 12);
+        } else {
+          bits = 0u;
+          for (int b = 0; base + b < n; ++b) bits |= (m[base + b] != 0 ? 1u : 0u) << b;
         }
+        w[i >> 1] |= bits << (16 * (i & 1));
       }
     }
   } else {
-    for (int u0 = 0; u0 < Td; u0 += 128) {
-      uint8_t b[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int u = u0 + i * 32 + lane;
-        b[i] = u < Td ? dmask[u] : 0;
-      }
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-        if (b[i]) {
-          const int u = u0 + i * 32 + lane;
-          f = min(f, u);
-          l = max(l, u);
-        }
-    }
+    for (int i = 0; i < W; ++i)
+      for (int b = 0; b < 32 && 32 * i + b < n; ++b) w[i] |= (m[32 * i + b] != 0 ? 1u : 0u) << b;
   }
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) {
-    f = min(f, __shfl_xor_sync(0xffffffffu, f, off));
-    l = max(l, __shfl_xor_sync(0xffffffffu, l, off));
-  }
-  first = f == INT32_MAX ? -1 : f;
-  leff = l + 1;
 }
 
-template <int M, int NT, int MAXMT, int S>
-struct Smem {
-  static constexpr int A_BYTES = MAXMT * M * ROWB;   // one K block of all M tiles
-  static constexpr int B_BYTES = NT * ROWB;          // one K block of the chunk
+template <int M, int NT, int MAXMT, int S, int R>
+struct Cfg {
+  static constexpr int A_BYTES = MAXMT * M * ROWB;  // one K block of all M tiles
+  static constexpr int B_BYTES = NT * ROWB;         // one K block of the chunk
   static constexpr int STAGE = A_BYTES + B_BYTES;
-  static constexpr int TILES = S * STAGE;
-  static constexpr int ACC_COLS = MAXMT * NT;        // TMEM columns per accumulator buffer
-  static constexpr int TMEM_COLS = 2 * ACC_COLS;     // double-buffered
-  static constexpr int DYN = TILES + 1024;           // + alignment slack
+  static constexpr int ACC_COLS = MAXMT * NT;       // TMEM columns per accumulator buffer
+  static constexpr int TMEM_COLS = 2 * ACC_COLS;    // double-buffered
+  static constexpr int DYN = S * STAGE + 1024;      // + alignment slack
+  static constexpr int HALF = NT / R;               // columns per epilogue thread per chunk
+  static_assert(R == 1 || (R == 2 && M == 64 && MAXMT == 1), "replication needs one 64-row tile");
+  static_assert(TMEM_COLS == 128 || TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM columns");
 };
 
-template <int M, int NT, int MAXMT, int S, bool ARGS>
+template <int M, int NT, int MAXMT, int S, int R, bool ARGS>
 __global__ void __launch_bounds__(NTHREADS, 1)
 tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB64,
                const __grid_constant__ CUtensorMap tmB16, TcParams P) {
-  using L = Smem<M, NT, MAXMT, S>;
-  static_assert(L::TMEM_COLS == 128 || L::TMEM_COLS == 256 || L::TMEM_COLS == 512, "TMEM cols");
+  using L = Cfg<M, NT, MAXMT, S, R>;
   extern __shared__ __align__(1024) unsigned char dsm[];
   __shared__ __align__(8) uint64_t full_bar[S];
   __shared__ __align__(8) uint64_t empty_bar[S];
   __shared__ __align__(8) uint64_t accf_bar[2];
   __shared__ __align__(8) uint64_t acce_bar[2];
+  __shared__ __align__(8) uint64_t metaf_bar[UQ];
+  __shared__ __align__(8) uint64_t metae_bar[UQ];
   __shared__ __align__(8) uint64_t epi_bar;  // epilogue-wide barrier (bounded, unlike bar.sync)
+  __shared__ UnitMeta meta[UQ];
   __shared__ uint32_t tmem_base_s;
   __shared__ volatile int abort_s;
   __shared__ float red_s[MAXMT * M];
-  __shared__ uint8_t tv_s[MAXMT * M];
+  __shared__ float half_mx[32];
+  __shared__ int half_ag[32];
+  __shared__ float half_s0[32];
 
   unsigned char* tiles = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(dsm) + 1023) & ~(uintptr_t)1023);
@@ -213,6 +228,10 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       ptx::mbar_init(&accf_bar[i], 1);
       ptx::mbar_init(&acce_bar[i], 4);  // one arrival per epilogue warp
     }
+    for (int i = 0; i < UQ; ++i) {
+      ptx::mbar_init(&metaf_bar[i], 1);
+      ptx::mbar_init(&metae_bar[i], 6);  // producer + MMA + 4 epilogue warps
+    }
     ptx::mbar_init(&epi_bar, 128);
     abort_s = 0;
     ptx::fence_barrier_init();
@@ -227,40 +246,100 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem_base = tmem_base_s;
+  const int64_t my_units = P.nunits > blockIdx.x ? (P.nunits - 1 - blockIdx.x) / gridDim.x + 1 : 0;
 
-  if (warp == 0) {
+  if (warp == SCHED_WARP) {
+    // ------------------------------------------------------------ scheduler
+    for (int64_t i0 = 0; i0 < my_units; i0 += 32) {
+      if (__any_sync(0xffffffffu, abort_s != 0)) break;  // warp-uniform exit
+      const int64_t i = i0 + lane;
+      UnitMeta m;
+      if (i < my_units) {
+        const TcUnit U = tc_decode(P, blockIdx.x + i * gridDim.x);
+        m.q_row0 = U.q_row0; m.d_row0 = U.d_row0;
+        m.out0 = U.out0; m.out_stride = U.out_stride;
+        m.arg0 = U.arg0; m.arg_stride = U.arg_stride;
+        m.dmask = U.dmask;
+        m.nq = U.nq; m.Tq = U.Tq; m.valid = U.valid ? 1 : 0; m.arg_rows = U.arg_rows;
+        m.pad = 0;
+        const int rows = U.nq * U.Tq;
+        mask_bits<QW_MAX>(U.qmask, rows < 32 * QW_MAX ? rows : 32 * QW_MAX, m.qw);
+        m.mw_ok = U.Td <= 32 * MW_MAX;
+        int first = -1, last = -1;
+        if (U.valid) {
+          mask_bits<MW_MAX>(U.dmask, U.Td < 32 * MW_MAX ? U.Td : 32 * MW_MAX, m.mw);
+#pragma unroll
+          for (int w = MW_MAX - 1; w >= 0; --w)
+            if (m.mw[w]) { first = 32 * w + __ffs(m.mw[w]) - 1; }
+#pragma unroll
+          for (int w = 0; w < MW_MAX; ++w)
+            if (m.mw[w]) { last = 32 * w + 31 - __clz(m.mw[w]); }
+          for (int u = 32 * MW_MAX; u < U.Td; ++u)  // long documents: mask tail scanned here
+            if (U.dmask == nullptr || U.dmask[u]) {
+              if (first < 0) first = u;
+              last = u;
+              if (U.dmask == nullptr) { last = U.Td - 1; break; }
+            }
+        } else {
+#pragma unroll
+          for (int w = 0; w < MW_MAX; ++w) m.mw[w] = 0u;
+        }
+        m.first = first;
+        m.leff = last + 1;
+      }
+      const int64_t nb = (my_units - i0) < 32 ? (my_units - i0) : 32;
+      for (int k = 0; k < nb; ++k) {
+        if (lane == k) {
+          const int64_t idx = i0 + k;
+          const int slot = (int)(idx % UQ);
+          const uint32_t par = (uint32_t)((idx / UQ) & 1);
+          if (ptx::mbar_wait(&metae_bar[slot], par ^ 1, &abort_s)) {
+            meta[slot] = m;
+            ptx::mbar_arrive(&metaf_bar[slot]);
+          }
+        }
+        __syncwarp();
+        if (__any_sync(0xffffffffu, abort_s != 0)) break;
+      }
+    }
+  } else if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     int stage = 0;
     uint32_t phase = 0;
-    for (int64_t v = blockIdx.x; v < P.nunits && !abort_s; v += gridDim.x) {
-      const TcUnit U = tc_decode(P, v);
-      if (!U.valid) continue;
-      int first, leff;
-      doc_extent(U.dmask, U.Td, first, leff);
-      const int rows = U.nq * U.Tq;
-      if (rows == 0) continue;
+    for (int64_t i = 0; i < my_units; ++i) {
+      const int slot = (int)(i % UQ);
+      if (!ptx::warp_wait(&metaf_bar[slot], (uint32_t)((i / UQ) & 1), &abort_s)) goto done;
+      const UnitMeta& m = meta[slot];
+      const int rows = m.nq * m.Tq;
       const int nmt = (rows + M - 1) / M;
-      const int nch = (leff + NT - 1) / NT;
+      const int nch = (m.valid && rows > 0) ? (m.leff + NT - 1) / NT : 0;
+      const int64_t q_row0 = m.q_row0, d_row0 = m.d_row0;
+      const int leff = m.leff;
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&metae_bar[slot]);
       for (int c = 0; c < nch; ++c) {
         const int u0 = c * NT;
         const int n = min(NT, leff - u0);
         const int nr = (n + 15) & ~15;
         for (int kb = 0; kb < P.KB; ++kb) {
-          if (!ptx::mbar_wait(&empty_bar[stage], phase ^ 1, &abort_s)) goto done;
+          if (!ptx::warp_wait(&empty_bar[stage], phase ^ 1, &abort_s)) goto done;
           if (lane == 0) {
             unsigned char* sA = tiles + stage * L::STAGE;
             unsigned char* sB = sA + L::A_BYTES;
             ptx::mbar_expect_tx(&full_bar[stage], (uint32_t)(nmt * M * ROWB + nr * ROWB));
-            for (int mt = 0; mt < nmt; ++mt)
-              ptx::tma_load_2d(sA + mt * M * ROWB, &tmA, kb * KBLK, (int)(U.q_row0 + mt * M),
-                               &full_bar[stage]);
+            if (R == 2) {  // the query twice: rows 0-31 and 32-63
+              ptx::tma_load_2d(sA, &tmA, kb * KBLK, (int)q_row0, &full_bar[stage]);
+              ptx::tma_load_2d(sA + 32 * ROWB, &tmA, kb * KBLK, (int)q_row0, &full_bar[stage]);
+            } else {
+              for (int mt = 0; mt < nmt; ++mt)
+                ptx::tma_load_2d(sA + mt * M * ROWB, &tmA, kb * KBLK, (int)(q_row0 + mt * M),
+                                 &full_bar[stage]);
+            }
             int r = 0;
             for (; r + 64 <= nr; r += 64)
-              ptx::tma_load_2d(sB + r * ROWB, &tmB64, kb * KBLK, (int)(U.d_row0 + u0 + r),
-                               &full_bar[stage]);
+              ptx::tma_load_2d(sB + r * ROWB, &tmB64, kb * KBLK, (int)(d_row0 + u0 + r), &full_bar[stage]);
             for (; r < nr; r += 16)
-              ptx::tma_load_2d(sB + r * ROWB, &tmB16, kb * KBLK, (int)(U.d_row0 + u0 + r),
-                               &full_bar[stage]);
+              ptx::tma_load_2d(sB + r * ROWB, &tmB16, kb * KBLK, (int)(d_row0 + u0 + r), &full_bar[stage]);
           }
           __syncwarp();
           if (++stage == S) { stage = 0; phase ^= 1; }
@@ -273,23 +352,24 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     uint32_t phase = 0;
     int as = 0;
     uint32_t aphase = 0;
-    for (int64_t v = blockIdx.x; v < P.nunits && !abort_s; v += gridDim.x) {
-      const TcUnit U = tc_decode(P, v);
-      if (!U.valid) continue;
-      int first, leff;
-      doc_extent(U.dmask, U.Td, first, leff);
-      const int rows = U.nq * U.Tq;
-      if (rows == 0) continue;
+    for (int64_t i = 0; i < my_units; ++i) {
+      const int slot = (int)(i % UQ);
+      if (!ptx::warp_wait(&metaf_bar[slot], (uint32_t)((i / UQ) & 1), &abort_s)) goto done;
+      const UnitMeta& m = meta[slot];
+      const int rows = m.nq * m.Tq;
       const int nmt = (rows + M - 1) / M;
-      const int nch = (leff + NT - 1) / NT;
+      const int nch = (m.valid && rows > 0) ? (m.leff + NT - 1) / NT : 0;
+      const int leff = m.leff;
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&metae_bar[slot]);
       for (int c = 0; c < nch; ++c) {
         const int n = min(NT, leff - c * NT);
         const int nr = (n + 15) & ~15;
         const uint32_t idesc = ptx::idesc_f16(P.fmt, M, nr);
-        if (!ptx::mbar_wait(&acce_bar[as], aphase ^ 1, &abort_s)) goto done;
+        if (!ptx::warp_wait(&acce_bar[as], aphase ^ 1, &abort_s)) goto done;
         ptx::tc_fence_after();
         for (int kb = 0; kb < P.KB; ++kb) {
-          if (!ptx::mbar_wait(&full_bar[stage], phase, &abort_s)) goto done;
+          if (!ptx::warp_wait(&full_bar[stage], phase, &abort_s)) goto done;
           ptx::tc_fence_after();
           if (lane == 0) {
             const uint32_t sA = ptx::smem_u32(tiles + stage * L::STAGE);
@@ -315,68 +395,84 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    using A = float;
-    const int sp = warp & 3;                       // TMEM subpartition of this warp
-    const int et = threadIdx.x - 64;               // 0..127
-    const int lr = (M == 128) ? sp * 32 + lane : (lane < 16 ? sp * 16 + lane : -1);
+    const int sp = warp & 3;   // TMEM subpartition of this warp
+    const int et = threadIdx.x - 64;  // 0..127
+    // row of the accumulator this thread reads, and its column half
+    const int lr = (M == 128) ? sp * 32 + lane
+                              : (lane < 16 ? (R == 2 ? (sp & 1) * 16 : sp * 16) + lane : -1);
+    const int h = (R == 2) ? (sp >> 1) : 0;
     int as = 0;
     uint32_t aphase = 0;
     uint32_t ephase = 0;
     float* scores = static_cast<float*>(p.scores);
-    for (int64_t v = blockIdx.x; v < P.nunits; v += gridDim.x) {
-      if (abort_s) break;
-      const TcUnit U = tc_decode(P, v);
-      if (!U.valid) {
-        if (et == 0) scores[U.out0] = (float)p.neg;
+    for (int64_t i = 0; i < my_units; ++i) {
+      const int slot = (int)(i % UQ);
+      if (!ptx::warp_wait(&metaf_bar[slot], (uint32_t)((i / UQ) & 1), &abort_s)) goto done;
+      const UnitMeta& m = meta[slot];
+      if (!m.valid) {
+        if (et == 0) scores[m.out0] = (float)p.neg;
         if (ARGS)
-          for (int t = et; t < U.arg_rows; t += 128) p.args[U.arg0 + t] = 0;
+          for (int t = et; t < m.arg_rows; t += 128) p.args[m.arg0 + t] = 0;
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&metae_bar[slot]);
         continue;
       }
-      int first, leff;
-      doc_extent(U.dmask, U.Td, first, leff);
-      const int rows = U.nq * U.Tq;
+      const int rows = m.nq * m.Tq;
       const int nmt = (rows + M - 1) / M;
-      const int nch = rows == 0 ? 0 : (leff + NT - 1) / NT;
-      A mx[MAXMT], s0[MAXMT];
+      const int nch = rows == 0 ? 0 : (m.leff + NT - 1) / NT;
+      const int first = m.first, leff = m.leff;
+      float mx[MAXMT], s0[MAXMT];
       int ag[MAXMT];
+      bool has_s0 = false;
 #pragma unroll
       for (int mt = 0; mt < MAXMT; ++mt) { mx[mt] = -INFINITY; ag[mt] = 0; s0[mt] = 0.f; }
       for (int c = 0; c < nch; ++c) {
         const int u0 = c * NT;
         const int n = min(NT, leff - u0);
-        uint32_t mw[NT / 32];
+        uint32_t mw[L::HALF / 32];
 #pragma unroll
-        for (int g = 0; g < NT / 32; ++g) {
-          const int cc = 32 * g + lane;
-          const bool ok = cc < n && (U.dmask == nullptr || U.dmask[u0 + cc] != 0);
-          mw[g] = __ballot_sync(0xffffffffu, ok);
+        for (int g = 0; g < L::HALF / 32; ++g) {
+          const int col0 = h * L::HALF + 32 * g;  // chunk column of this group
+          uint32_t w;
+          if (m.mw_ok) {
+            w = (u0 + col0) < 32 * MW_MAX ? m.mw[(u0 + col0) >> 5] : 0u;
+          } else {
+            const int cc = col0 + lane;
+            const bool ok = cc < n && (m.dmask == nullptr || m.dmask[u0 + cc] != 0);
+            w = __ballot_sync(0xffffffffu, ok);
+          }
+          const int lim = n - col0;
+          mw[g] = lim >= 32 ? w : (lim > 0 ? w & ((1u << lim) - 1u) : 0u);
         }
-        if (!ptx::mbar_wait(&accf_bar[as], aphase, &abort_s)) goto done;
+        if (!ptx::warp_wait(&accf_bar[as], aphase, &abort_s)) goto done;
         ptx::tc_fence_after();
         const uint32_t tb = tmem_base + ((uint32_t)(sp * 32) << 16) + (uint32_t)(as * L::ACC_COLS);
 #pragma unroll
         for (int mt = 0; mt < MAXMT; ++mt) {
           if (mt < nmt) {
 #pragma unroll
-            for (int g = 0; g < NT / 32; ++g) {
-              if (32 * g < n) {
+            for (int g = 0; g < L::HALF / 32; ++g) {
+              const int col0 = h * L::HALF + 32 * g;
+              if (col0 < n) {
                 uint32_t r[32];
-                ptx::tmem_ld32(tb + mt * NT + 32 * g, r);
+                ptx::tmem_ld32(tb + mt * NT + col0, r);
                 ptx::tmem_wait_ld();
-                const uint32_t m = mw[g];
+                const uint32_t mm = mw[g];
 #pragma unroll
                 for (int cc = 0; cc < 32; ++cc) {
-                  const A s = __uint_as_float(r[cc]);
-                  if (((m >> cc) & 1u) && s > mx[mt]) {
+                  const float s = __uint_as_float(r[cc]);
+                  if (((mm >> cc) & 1u) && s > mx[mt]) {
                     mx[mt] = s;
-                    ag[mt] = u0 + 32 * g + cc + 1;
+                    ag[mt] = u0 + col0 + cc + 1;
                   }
                 }
               }
             }
-            if (first >= u0 && first < u0 + NT) {
+            const int fc = first - u0 - h * L::HALF;  // first valid column, in my half?
+            if (fc >= 0 && fc < L::HALF && first - u0 < n) {
               s0[mt] = __uint_as_float(ptx::tmem_ld1(tb + mt * NT + (first - u0)));
               ptx::tmem_wait_ld();
+              has_s0 = true;
             }
           }
         }
@@ -386,41 +482,58 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         as ^= 1;
         if (as == 0) aphase ^= 1;
       }
+      if (R == 2) {
+        // the second copy of rows 0-31 (columns of the upper half) hands its state over
+        if (h == 1 && lr >= 0) {
+          half_mx[lr] = mx[0];
+          half_ag[lr] = ag[0];
+          half_s0[lr] = has_s0 ? s0[0] : __int_as_float(0x7fc00001);
+        }
+        ptx::mbar_arrive(&epi_bar);
+        if (!ptx::warp_wait(&epi_bar, ephase, &abort_s)) goto done;
+        ephase ^= 1;
+        if (h == 0 && lr >= 0) {
+          merge_state(mx[0], ag[0], half_mx[lr], half_ag[lr]);
+          if (!has_s0) s0[0] = half_s0[lr];
+        }
+      }
       // finish the rows: exact first-valid rule, tape, per-row contribution
 #pragma unroll
       for (int mt = 0; mt < MAXMT; ++mt) {
         const int r = mt * M + lr;
-        if (mt < nmt && lr >= 0 && r < rows) {
-          const int qi = r / U.Tq, t = r - qi * U.Tq;
-          const bool tv = U.qmask == nullptr || U.qmask[r] != 0;
-          A m = mx[mt];
+        if (mt < nmt && lr >= 0 && h == 0 && r < rows) {
+          const int qi = r / m.Tq, t = r - qi * m.Tq;
+          const bool tv = (m.qw[r >> 5] >> (r & 31)) & 1u;
+          float v = mx[mt];
           int a = ag[mt];
-          final_fixup(m, a, first, s0[mt]);
+          final_fixup(v, a, first, s0[mt]);
           const bool ok = tv && a > 0;
-          red_s[r] = ok ? m : 0.f;
-          tv_s[r] = tv ? 1 : 0;
-          if (ARGS) p.args[U.arg0 + qi * U.arg_stride + t] = ok ? a : 0;
+          red_s[r] = ok ? v : 0.f;
+          if (ARGS) p.args[m.arg0 + qi * m.arg_stride + t] = ok ? a : 0;
         }
       }
       ptx::mbar_arrive(&epi_bar);
-      if (!ptx::mbar_wait(&epi_bar, ephase, &abort_s)) goto done;
+      if (!ptx::warp_wait(&epi_bar, ephase, &abort_s)) goto done;
       ephase ^= 1;
-      if (et < U.nq) {
+      if (et < m.nq) {
         const int qi = et;
-        A score = 0.f;
+        float score = 0.f;
         int nvalid = 0;
 #pragma unroll 8
-        for (int t = 0; t < U.Tq; ++t) {  // Sigma_t in t order (forward_pair.jl:92-95)
-          score += red_s[qi * U.Tq + t];
-          nvalid += tv_s[qi * U.Tq + t];
+        for (int t = 0; t < m.Tq; ++t) {  // Sigma_t in t order (forward_pair.jl:92-95)
+          const int r = qi * m.Tq + t;
+          score += red_s[r];
+          nvalid += (m.qw[r >> 5] >> (r & 31)) & 1u;
         }
         if (p.normalize) score = score * (1.0f / (float)(nvalid > 1 ? nvalid : 1));
-        scores[U.out0 + qi * U.out_stride] = score;
+        scores[m.out0 + qi * m.out_stride] = score;
       }
       if (ARGS)
-        for (int t = U.Tq + et; t < U.arg_rows; t += 128) p.args[U.arg0 + t] = 0;
-      ptx::mbar_arrive(&epi_bar);  // red_s is reused by the next unit
-      if (!ptx::mbar_wait(&epi_bar, ephase, &abort_s)) goto done;
+        for (int t = m.Tq + et; t < m.arg_rows; t += 128) p.args[m.arg0 + t] = 0;
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&metae_bar[slot]);
+      ptx::mbar_arrive(&epi_bar);  // red_s / half_* are reused by the next unit
+      if (!ptx::warp_wait(&epi_bar, ephase, &abort_s)) goto done;
       ephase ^= 1;
     }
   }
@@ -492,26 +605,37 @@ static void plan(const ScanParams& p, int& G, int& rows) {
   rows = G * Tq;
 }
 
-template <int M, int NT, int MAXMT, int S>
+template <int M, int NT, int MAXMT, int S, int R>
 static cudaError_t launch_cfg(const TcParams& P, const CUtensorMap& a, const CUtensorMap& b64,
                               const CUtensorMap& b16, cudaStream_t s, int ctas_per_sm) {
-  using L = Smem<M, NT, MAXMT, S>;
+  using L = Cfg<M, NT, MAXMT, S, R>;
   int64_t grid = (int64_t)device_sm_count() * ctas_per_sm;
   if (grid > P.nunits) grid = P.nunits;
   if (grid < 1) grid = 1;
   cudaError_t e;
   if (P.p.args) {
-    auto k = tc_scan_kernel<M, NT, MAXMT, S, true>;
+    auto k = tc_scan_kernel<M, NT, MAXMT, S, R, true>;
     if ((e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, L::DYN)) != cudaSuccess)
       return e;
     k<<<(unsigned)grid, NTHREADS, L::DYN, s>>>(a, b64, b16, P);
   } else {
-    auto k = tc_scan_kernel<M, NT, MAXMT, S, false>;
+    auto k = tc_scan_kernel<M, NT, MAXMT, S, R, false>;
     if ((e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, L::DYN)) != cudaSuccess)
       return e;
     k<<<(unsigned)grid, NTHREADS, L::DYN, s>>>(a, b64, b16, P);
   }
   return cudaGetLastError();
+}
+
+// Engine tile width override for tuning (FMS_TC_NT=128|256); 0 = automatic.
+static int nt_override() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("FMS_TC_NT");
+    v = e ? atoi(e) : 0;
+    if (v != 128 && v != 256) v = 0;
+  }
+  return v;
 }
 
 }  // namespace tc
@@ -559,14 +683,23 @@ cudaError_t launch_scan_tc(int dtype, const ScanParams& p, cudaStream_t s) {
   P.KB = p.dim / tc::KBLK;
   P.fmt = dtype == FMS_BF16 ? 1u : 0u;
   if (P.nunits == 0) return cudaSuccess;
+  const bool rep = rows <= 32;
   const int M = rows <= 64 ? 64 : 128;
   CUtensorMap a, b64, b16;
-  if (!tc::make_map(&a, p.Q, P.fmt, p.dim, p.nq_tok, M)) return cudaErrorNotSupported;
+  if (!tc::make_map(&a, p.Q, P.fmt, p.dim, p.nq_tok, rep ? 32 : M)) return cudaErrorNotSupported;
   if (!tc::make_map(&b64, p.D, P.fmt, p.dim, p.nd_tok, 64)) return cudaErrorNotSupported;
   if (!tc::make_map(&b16, p.D, P.fmt, p.dim, p.nd_tok, 16)) return cudaErrorNotSupported;
-  if (rows <= 64) return tc::launch_cfg<64, 128, 1, 4>(P, a, b64, b16, s, 2);
-  if (rows <= 128) return tc::launch_cfg<128, 128, 1, 3>(P, a, b64, b16, s, 2);
-  return tc::launch_cfg<128, 128, 2, 4>(P, a, b64, b16, s, 1);
+  const int nt = tc::nt_override();
+  if (rep) {
+    if (nt == 128) return tc::launch_cfg<64, 128, 1, 4, 2>(P, a, b64, b16, s, 2);
+    return tc::launch_cfg<64, 256, 1, 5, 2>(P, a, b64, b16, s, 1);
+  }
+  if (rows <= 64) {
+    if (nt == 128) return tc::launch_cfg<64, 128, 1, 4, 1>(P, a, b64, b16, s, 2);
+    return tc::launch_cfg<64, 256, 1, 5, 1>(P, a, b64, b16, s, 1);
+  }
+  if (rows <= 128) return tc::launch_cfg<128, 128, 1, 3, 1>(P, a, b64, b16, s, 2);
+  return tc::launch_cfg<128, 128, 2, 4, 1>(P, a, b64, b16, s, 1);
 }
 
 }  // namespace fms
