@@ -82,7 +82,7 @@ struct TcUnit {
 struct UnitMeta {
   int64_t q_row0, d_row0, out0, out_stride, arg0, arg_stride;
   const uint8_t* dmask;   // kept for documents longer than 32*MW_MAX tokens
-  int nq, Tq, leff, first, valid, arg_rows, mw_ok, pad;
+  int nq, Tq, leff, first, valid, arg_rows, mw_ok, aflags;  // aflags bit0: load a new query tile
   uint32_t mw[MW_MAX];    // bit u: document token u valid (u < 32*MW_MAX)
   uint32_t qw[QW_MAX];    // bit r: query row r valid
 };
@@ -179,27 +179,52 @@ __device__ __forceinline__ void mask_bits(const uint8_t* m, int n, uint32_t (&w)
   }
 }
 
-template <int M, int NT, int MAXMT, int S, int R>
+
+// Shared-memory plan of one engine configuration.  ARES: the query tile of a unit
+// (all K blocks) stays resident in one of two slots and is re-loaded only when
+// the next unit's query differs; the S-stage ring then carries document rows
+// only.  Without ARES (large dim) every stage carries its K block of both.
+template <int M, int NT, int MAXMT, int S, int R, bool ARES>
 struct Cfg {
   static constexpr int A_BYTES = MAXMT * M * ROWB;  // one K block of all M tiles
   static constexpr int B_BYTES = NT * ROWB;         // one K block of the chunk
-  static constexpr int STAGE = A_BYTES + B_BYTES;
+  static constexpr int STAGE = (ARES ? 0 : A_BYTES) + B_BYTES;
   static constexpr int ACC_COLS = MAXMT * NT;       // TMEM columns per accumulator buffer
   static constexpr int TMEM_COLS = 2 * ACC_COLS;    // double-buffered
-  static constexpr int DYN = S * STAGE + 1024;      // + alignment slack
   static constexpr int HALF = NT / R;               // columns per epilogue thread per chunk
+  static constexpr bool EARLY = MAXMT * HALF <= 64; // copy the whole chunk to registers first
+  static int dyn_bytes(int KB) { return (ARES ? 2 * KB * A_BYTES : 0) + S * STAGE + 1024; }
   static_assert(R == 1 || (R == 2 && M == 64 && MAXMT == 1), "replication needs one 64-row tile");
   static_assert(TMEM_COLS == 128 || TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM columns");
 };
 
-template <int M, int NT, int MAXMT, int S, int R, bool ARGS>
+struct BMaps {
+  CUtensorMap b128, b64, b32, b16;  // document rows, boxes of 128 / 64 / 32 / 16 rows
+};
+
+// Document rows [row, row + nr) of one K block (nr a multiple of 16, <= 128)
+// with at most three boxes.
+__device__ __forceinline__ void load_doc_rows(unsigned char* sB, const BMaps& bm, int x, int64_t row,
+                                              int nr, uint64_t* bar) {
+  int r = 0;
+  if (nr == 128) {
+    ptx::tma_load_2d(sB, &bm.b128, x, (int)row, bar);
+    return;
+  }
+  if (nr - r >= 64) { ptx::tma_load_2d(sB + r * ROWB, &bm.b64, x, (int)(row + r), bar); r += 64; }
+  if (nr - r >= 32) { ptx::tma_load_2d(sB + r * ROWB, &bm.b32, x, (int)(row + r), bar); r += 32; }
+  if (nr - r >= 16) { ptx::tma_load_2d(sB + r * ROWB, &bm.b16, x, (int)(row + r), bar); r += 16; }
+}
+
+template <int M, int NT, int MAXMT, int S, int R, bool ARES, bool ARGS>
 __global__ void __launch_bounds__(NTHREADS, 1)
-tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB64,
-               const __grid_constant__ CUtensorMap tmB16, TcParams P) {
-  using L = Cfg<M, NT, MAXMT, S, R>;
+tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ BMaps bm, TcParams P) {
+  using L = Cfg<M, NT, MAXMT, S, R, ARES>;
   extern __shared__ __align__(1024) unsigned char dsm[];
   __shared__ __align__(8) uint64_t full_bar[S];
   __shared__ __align__(8) uint64_t empty_bar[S];
+  __shared__ __align__(8) uint64_t afull_bar[2];
+  __shared__ __align__(8) uint64_t aempty_bar[2];
   __shared__ __align__(8) uint64_t accf_bar[2];
   __shared__ __align__(8) uint64_t acce_bar[2];
   __shared__ __align__(8) uint64_t metaf_bar[UQ];
@@ -215,6 +240,8 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 
   unsigned char* tiles = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(dsm) + 1023) & ~(uintptr_t)1023);
+  unsigned char* aslots = tiles;                                          // ARES only
+  unsigned char* ring = tiles + (ARES ? 2 * P.KB * L::A_BYTES : 0);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const ScanParams& p = P.p;
@@ -225,6 +252,8 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       ptx::mbar_init(&empty_bar[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
+      ptx::mbar_init(&afull_bar[i], 1);
+      ptx::mbar_init(&aempty_bar[i], 1);
       ptx::mbar_init(&accf_bar[i], 1);
       ptx::mbar_init(&acce_bar[i], 4);  // one arrival per epilogue warp
     }
@@ -238,8 +267,10 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   }
   if (warp == 0 && lane == 0) {
     ptx::prefetch_tmap(&tmA);
-    ptx::prefetch_tmap(&tmB64);
-    ptx::prefetch_tmap(&tmB16);
+    ptx::prefetch_tmap(&bm.b128);
+    ptx::prefetch_tmap(&bm.b64);
+    ptx::prefetch_tmap(&bm.b32);
+    ptx::prefetch_tmap(&bm.b16);
   }
   if (warp == 1) ptx::tmem_alloc(&tmem_base_s, L::TMEM_COLS);
   ptx::tc_fence_before();
@@ -250,10 +281,13 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 
   if (warp == SCHED_WARP) {
     // ------------------------------------------------------------ scheduler
+    int have_prev = 0;       // warp-uniform: last working unit's query run
+    int64_t prev_q = -1;
     for (int64_t i0 = 0; i0 < my_units; i0 += 32) {
       if (__any_sync(0xffffffffu, abort_s != 0)) break;  // warp-uniform exit
       const int64_t i = i0 + lane;
       UnitMeta m;
+      int working = 0;
       if (i < my_units) {
         const TcUnit U = tc_decode(P, blockIdx.x + i * gridDim.x);
         m.q_row0 = U.q_row0; m.d_row0 = U.d_row0;
@@ -261,7 +295,6 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         m.arg0 = U.arg0; m.arg_stride = U.arg_stride;
         m.dmask = U.dmask;
         m.nq = U.nq; m.Tq = U.Tq; m.valid = U.valid ? 1 : 0; m.arg_rows = U.arg_rows;
-        m.pad = 0;
         const int rows = U.nq * U.Tq;
         mask_bits<QW_MAX>(U.qmask, rows < 32 * QW_MAX ? rows : 32 * QW_MAX, m.qw);
         m.mw_ok = U.Td <= 32 * MW_MAX;
@@ -286,7 +319,21 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         }
         m.first = first;
         m.leff = last + 1;
+        working = (m.valid && rows > 0 && m.leff > 0) ? 1 : 0;
       }
+      // a new query tile is needed when a working unit's query run differs from
+      // the previous working unit's (scanned in unit order across the warp)
+      int anew = 0;
+      for (int k = 0; k < 32; ++k) {
+        const int wk = __shfl_sync(0xffffffffu, working, k);
+        const long long qk = __shfl_sync(0xffffffffu, (long long)(working ? m.q_row0 : 0), k);
+        if (wk) {
+          if (lane == k) anew = (!have_prev || qk != prev_q) ? 1 : 0;
+          have_prev = 1;
+          prev_q = qk;
+        }
+      }
+      m.aflags = anew;
       const int64_t nb = (my_units - i0) < 32 ? (my_units - i0) : 32;
       for (int k = 0; k < nb; ++k) {
         if (lane == k) {
@@ -306,6 +353,8 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     // ------------------------------------------------------------ TMA producer
     int stage = 0;
     uint32_t phase = 0;
+    int aslot = 1;           // ARES: slot of the current query tile
+    uint32_t aphase = 1;     // flips when aslot wraps to 0
     for (int64_t i = 0; i < my_units; ++i) {
       const int slot = (int)(i % UQ);
       if (!ptx::warp_wait(&metaf_bar[slot], (uint32_t)((i / UQ) & 1), &abort_s)) goto done;
@@ -315,8 +364,30 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       const int nch = (m.valid && rows > 0) ? (m.leff + NT - 1) / NT : 0;
       const int64_t q_row0 = m.q_row0, d_row0 = m.d_row0;
       const int leff = m.leff;
+      const int anew = m.aflags & 1;
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(&metae_bar[slot]);
+      if (ARES && anew) {
+        aslot ^= 1;
+        if (aslot == 0) aphase ^= 1;
+        if (!ptx::warp_wait(&aempty_bar[aslot], aphase ^ 1, &abort_s)) goto done;
+        if (lane == 0) {
+          unsigned char* sA = aslots + aslot * P.KB * L::A_BYTES;
+          ptx::mbar_expect_tx(&afull_bar[aslot], (uint32_t)(P.KB * nmt * M * ROWB));
+          for (int kb = 0; kb < P.KB; ++kb) {
+            unsigned char* sAk = sA + kb * L::A_BYTES;
+            if (R == 2) {  // the query twice: rows 0-31 and 32-63
+              ptx::tma_load_2d(sAk, &tmA, kb * KBLK, (int)q_row0, &afull_bar[aslot]);
+              ptx::tma_load_2d(sAk + 32 * ROWB, &tmA, kb * KBLK, (int)q_row0, &afull_bar[aslot]);
+            } else {
+              for (int mt = 0; mt < nmt; ++mt)
+                ptx::tma_load_2d(sAk + mt * M * ROWB, &tmA, kb * KBLK, (int)(q_row0 + mt * M),
+                                 &afull_bar[aslot]);
+            }
+          }
+        }
+        __syncwarp();
+      }
       for (int c = 0; c < nch; ++c) {
         const int u0 = c * NT;
         const int n = min(NT, leff - u0);
@@ -324,22 +395,20 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         for (int kb = 0; kb < P.KB; ++kb) {
           if (!ptx::warp_wait(&empty_bar[stage], phase ^ 1, &abort_s)) goto done;
           if (lane == 0) {
-            unsigned char* sA = tiles + stage * L::STAGE;
-            unsigned char* sB = sA + L::A_BYTES;
-            ptx::mbar_expect_tx(&full_bar[stage], (uint32_t)(nmt * M * ROWB + nr * ROWB));
-            if (R == 2) {  // the query twice: rows 0-31 and 32-63
-              ptx::tma_load_2d(sA, &tmA, kb * KBLK, (int)q_row0, &full_bar[stage]);
-              ptx::tma_load_2d(sA + 32 * ROWB, &tmA, kb * KBLK, (int)q_row0, &full_bar[stage]);
-            } else {
-              for (int mt = 0; mt < nmt; ++mt)
-                ptx::tma_load_2d(sA + mt * M * ROWB, &tmA, kb * KBLK, (int)(q_row0 + mt * M),
-                                 &full_bar[stage]);
+            unsigned char* st = ring + stage * L::STAGE;
+            unsigned char* sB = st + (ARES ? 0 : L::A_BYTES);
+            ptx::mbar_expect_tx(&full_bar[stage], (uint32_t)((ARES ? 0 : nmt * M * ROWB) + nr * ROWB));
+            if (!ARES) {
+              if (R == 2) {
+                ptx::tma_load_2d(st, &tmA, kb * KBLK, (int)q_row0, &full_bar[stage]);
+                ptx::tma_load_2d(st + 32 * ROWB, &tmA, kb * KBLK, (int)q_row0, &full_bar[stage]);
+              } else {
+                for (int mt = 0; mt < nmt; ++mt)
+                  ptx::tma_load_2d(st + mt * M * ROWB, &tmA, kb * KBLK, (int)(q_row0 + mt * M),
+                                   &full_bar[stage]);
+              }
             }
-            int r = 0;
-            for (; r + 64 <= nr; r += 64)
-              ptx::tma_load_2d(sB + r * ROWB, &tmB64, kb * KBLK, (int)(d_row0 + u0 + r), &full_bar[stage]);
-            for (; r < nr; r += 16)
-              ptx::tma_load_2d(sB + r * ROWB, &tmB16, kb * KBLK, (int)(d_row0 + u0 + r), &full_bar[stage]);
+            load_doc_rows(sB, bm, kb * KBLK, d_row0 + u0, nr, &full_bar[stage]);
           }
           __syncwarp();
           if (++stage == S) { stage = 0; phase ^= 1; }
@@ -352,6 +421,9 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     uint32_t phase = 0;
     int as = 0;
     uint32_t aphase = 0;
+    int aslot = 1;
+    uint32_t aslot_phase = 1;
+    bool holding = false;    // ARES: an A slot is in use (released on the next switch)
     for (int64_t i = 0; i < my_units; ++i) {
       const int slot = (int)(i % UQ);
       if (!ptx::warp_wait(&metaf_bar[slot], (uint32_t)((i / UQ) & 1), &abort_s)) goto done;
@@ -360,8 +432,17 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       const int nmt = (rows + M - 1) / M;
       const int nch = (m.valid && rows > 0) ? (m.leff + NT - 1) / NT : 0;
       const int leff = m.leff;
+      const int anew = m.aflags & 1;
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(&metae_bar[slot]);
+      if (ARES && anew) {
+        if (holding && lane == 0) ptx::mma_commit(&aempty_bar[aslot]);  // after its last MMA
+        aslot ^= 1;
+        if (aslot == 0) aslot_phase ^= 1;
+        if (!ptx::warp_wait(&afull_bar[aslot], aslot_phase, &abort_s)) goto done;
+        ptx::tc_fence_after();
+        holding = true;
+      }
       for (int c = 0; c < nch; ++c) {
         const int n = min(NT, leff - c * NT);
         const int nr = (n + 15) & ~15;
@@ -372,8 +453,9 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           if (!ptx::warp_wait(&full_bar[stage], phase, &abort_s)) goto done;
           ptx::tc_fence_after();
           if (lane == 0) {
-            const uint32_t sA = ptx::smem_u32(tiles + stage * L::STAGE);
-            const uint32_t sB = sA + L::A_BYTES;
+            const uint32_t st = ptx::smem_u32(ring + stage * L::STAGE);
+            const uint32_t sA = ARES ? ptx::smem_u32(aslots + (aslot * P.KB + kb) * L::A_BYTES) : st;
+            const uint32_t sB = st + (ARES ? 0 : L::A_BYTES);
             const uint64_t bdesc = ptx::sw128_desc(sB);
             for (int mt = 0; mt < nmt; ++mt) {
               const uint64_t adesc = ptx::sw128_desc(sA + mt * M * ROWB);
@@ -447,38 +529,79 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         if (!ptx::warp_wait(&accf_bar[as], aphase, &abort_s)) goto done;
         ptx::tc_fence_after();
         const uint32_t tb = tmem_base + ((uint32_t)(sp * 32) << 16) + (uint32_t)(as * L::ACC_COLS);
+        const int fc = first - u0 - h * L::HALF;  // first valid column, in my half?
+        const bool s0_here = fc >= 0 && fc < L::HALF && first - u0 < n;
+        if (L::EARLY) {
+          // copy the chunk to registers and hand the accumulator back at once
+          uint32_t r[MAXMT][L::HALF / 32][32];
+          uint32_t r0[MAXMT];
 #pragma unroll
-        for (int mt = 0; mt < MAXMT; ++mt) {
-          if (mt < nmt) {
+          for (int mt = 0; mt < MAXMT; ++mt) {
+            if (mt < nmt) {
 #pragma unroll
-            for (int g = 0; g < L::HALF / 32; ++g) {
-              const int col0 = h * L::HALF + 32 * g;
-              if (col0 < n) {
-                uint32_t r[32];
-                ptx::tmem_ld32(tb + mt * NT + col0, r);
-                ptx::tmem_wait_ld();
-                const uint32_t mm = mw[g];
+              for (int g = 0; g < L::HALF / 32; ++g)
+                if (h * L::HALF + 32 * g < n) ptx::tmem_ld32(tb + mt * NT + h * L::HALF + 32 * g, r[mt][g]);
+              if (s0_here) r0[mt] = ptx::tmem_ld1(tb + mt * NT + (first - u0));
+            }
+          }
+          ptx::tmem_wait_ld();
+          ptx::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) ptx::mbar_arrive(&acce_bar[as]);
 #pragma unroll
-                for (int cc = 0; cc < 32; ++cc) {
-                  const float s = __uint_as_float(r[cc]);
-                  if (((mm >> cc) & 1u) && s > mx[mt]) {
-                    mx[mt] = s;
-                    ag[mt] = u0 + col0 + cc + 1;
+          for (int mt = 0; mt < MAXMT; ++mt) {
+            if (mt < nmt) {
+#pragma unroll
+              for (int g = 0; g < L::HALF / 32; ++g) {
+                const int col0 = h * L::HALF + 32 * g;
+                if (col0 < n) {
+                  const uint32_t mm = mw[g];
+#pragma unroll
+                  for (int cc = 0; cc < 32; ++cc) {
+                    const float s = __uint_as_float(r[mt][g][cc]);
+                    if (((mm >> cc) & 1u) && s > mx[mt]) {
+                      mx[mt] = s;
+                      ag[mt] = u0 + col0 + cc + 1;
+                    }
                   }
                 }
               }
-            }
-            const int fc = first - u0 - h * L::HALF;  // first valid column, in my half?
-            if (fc >= 0 && fc < L::HALF && first - u0 < n) {
-              s0[mt] = __uint_as_float(ptx::tmem_ld1(tb + mt * NT + (first - u0)));
-              ptx::tmem_wait_ld();
-              has_s0 = true;
+              if (s0_here) { s0[mt] = __uint_as_float(r0[mt]); has_s0 = true; }
             }
           }
+        } else {
+#pragma unroll
+          for (int mt = 0; mt < MAXMT; ++mt) {
+            if (mt < nmt) {
+#pragma unroll
+              for (int g = 0; g < L::HALF / 32; ++g) {
+                const int col0 = h * L::HALF + 32 * g;
+                if (col0 < n) {
+                  uint32_t r[32];
+                  ptx::tmem_ld32(tb + mt * NT + col0, r);
+                  ptx::tmem_wait_ld();
+                  const uint32_t mm = mw[g];
+#pragma unroll
+                  for (int cc = 0; cc < 32; ++cc) {
+                    const float s = __uint_as_float(r[cc]);
+                    if (((mm >> cc) & 1u) && s > mx[mt]) {
+                      mx[mt] = s;
+                      ag[mt] = u0 + col0 + cc + 1;
+                    }
+                  }
+                }
+              }
+              if (s0_here) {
+                s0[mt] = __uint_as_float(ptx::tmem_ld1(tb + mt * NT + (first - u0)));
+                ptx::tmem_wait_ld();
+                has_s0 = true;
+              }
+            }
+          }
+          ptx::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) ptx::mbar_arrive(&acce_bar[as]);
         }
-        ptx::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(&acce_bar[as]);
         as ^= 1;
         if (as == 0) aphase ^= 1;
       }
@@ -605,37 +728,27 @@ static void plan(const ScanParams& p, int& G, int& rows) {
   rows = G * Tq;
 }
 
-template <int M, int NT, int MAXMT, int S, int R>
-static cudaError_t launch_cfg(const TcParams& P, const CUtensorMap& a, const CUtensorMap& b64,
-                              const CUtensorMap& b16, cudaStream_t s, int ctas_per_sm) {
-  using L = Cfg<M, NT, MAXMT, S, R>;
+template <int M, int NT, int MAXMT, int S, int R, bool ARES>
+static cudaError_t launch_cfg(const TcParams& P, const CUtensorMap& a, const BMaps& bm, cudaStream_t s,
+                              int ctas_per_sm) {
+  using L = Cfg<M, NT, MAXMT, S, R, ARES>;
   int64_t grid = (int64_t)device_sm_count() * ctas_per_sm;
   if (grid > P.nunits) grid = P.nunits;
   if (grid < 1) grid = 1;
+  const int dyn = L::dyn_bytes(P.KB);
   cudaError_t e;
   if (P.p.args) {
-    auto k = tc_scan_kernel<M, NT, MAXMT, S, R, true>;
-    if ((e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, L::DYN)) != cudaSuccess)
+    auto k = tc_scan_kernel<M, NT, MAXMT, S, R, ARES, true>;
+    if ((e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn)) != cudaSuccess)
       return e;
-    k<<<(unsigned)grid, NTHREADS, L::DYN, s>>>(a, b64, b16, P);
+    k<<<(unsigned)grid, NTHREADS, dyn, s>>>(a, bm, P);
   } else {
-    auto k = tc_scan_kernel<M, NT, MAXMT, S, R, false>;
-    if ((e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, L::DYN)) != cudaSuccess)
+    auto k = tc_scan_kernel<M, NT, MAXMT, S, R, ARES, false>;
+    if ((e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn)) != cudaSuccess)
       return e;
-    k<<<(unsigned)grid, NTHREADS, L::DYN, s>>>(a, b64, b16, P);
+    k<<<(unsigned)grid, NTHREADS, dyn, s>>>(a, bm, P);
   }
   return cudaGetLastError();
-}
-
-// Engine tile width override for tuning (FMS_TC_NT=128|256); 0 = automatic.
-static int nt_override() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("FMS_TC_NT");
-    v = e ? atoi(e) : 0;
-    if (v != 128 && v != 256) v = 0;
-  }
-  return v;
 }
 
 }  // namespace tc
@@ -685,21 +798,31 @@ cudaError_t launch_scan_tc(int dtype, const ScanParams& p, cudaStream_t s) {
   if (P.nunits == 0) return cudaSuccess;
   const bool rep = rows <= 32;
   const int M = rows <= 64 ? 64 : 128;
-  CUtensorMap a, b64, b16;
+  CUtensorMap a;
+  tc::BMaps bm;
   if (!tc::make_map(&a, p.Q, P.fmt, p.dim, p.nq_tok, rep ? 32 : M)) return cudaErrorNotSupported;
-  if (!tc::make_map(&b64, p.D, P.fmt, p.dim, p.nd_tok, 64)) return cudaErrorNotSupported;
-  if (!tc::make_map(&b16, p.D, P.fmt, p.dim, p.nd_tok, 16)) return cudaErrorNotSupported;
-  const int nt = tc::nt_override();
+  if (!tc::make_map(&bm.b128, p.D, P.fmt, p.dim, p.nd_tok, 128) ||
+      !tc::make_map(&bm.b64, p.D, P.fmt, p.dim, p.nd_tok, 64) ||
+      !tc::make_map(&bm.b32, p.D, P.fmt, p.dim, p.nd_tok, 32) ||
+      !tc::make_map(&bm.b16, p.D, P.fmt, p.dim, p.nd_tok, 16))
+    return cudaErrorNotSupported;
+  // The query tile stays resident when both slots fit next to the ring.
+  const bool small_k = P.KB <= 2;   // dim <= 128
+  const bool mid_k = P.KB <= 4;     // dim <= 256
   if (rep) {
-    if (nt == 128) return tc::launch_cfg<64, 128, 1, 4, 2>(P, a, b64, b16, s, 2);
-    return tc::launch_cfg<64, 256, 1, 5, 2>(P, a, b64, b16, s, 1);
+    if (mid_k) return tc::launch_cfg<64, 128, 1, 4, 2, true>(P, a, bm, s, small_k ? 2 : 1);
+    return tc::launch_cfg<64, 128, 1, 4, 2, false>(P, a, bm, s, 2);
   }
   if (rows <= 64) {
-    if (nt == 128) return tc::launch_cfg<64, 128, 1, 4, 1>(P, a, b64, b16, s, 2);
-    return tc::launch_cfg<64, 256, 1, 5, 1>(P, a, b64, b16, s, 1);
+    if (mid_k) return tc::launch_cfg<64, 128, 1, 4, 1, true>(P, a, bm, s, small_k ? 2 : 1);
+    return tc::launch_cfg<64, 128, 1, 4, 1, false>(P, a, bm, s, 2);
   }
-  if (rows <= 128) return tc::launch_cfg<128, 128, 1, 3, 1>(P, a, b64, b16, s, 2);
-  return tc::launch_cfg<128, 128, 2, 4, 1>(P, a, b64, b16, s, 1);
+  if (rows <= 128) {
+    if (small_k) return tc::launch_cfg<128, 128, 1, 8, 1, true>(P, a, bm, s, 1);
+    return tc::launch_cfg<128, 128, 1, 3, 1, false>(P, a, bm, s, 2);
+  }
+  if (small_k) return tc::launch_cfg<128, 128, 2, 5, 1, true>(P, a, bm, s, 1);
+  return tc::launch_cfg<128, 128, 2, 4, 1, false>(P, a, bm, s, 1);
 }
 
 }  // namespace fms
