@@ -14,7 +14,9 @@ from pathlib import Path
 import torch
 
 PKG = Path(__file__).resolve().parent
-LIB_PATH = PKG / "libflashmaxsim_sm100.so"
+# FMS_LIBRARY overrides the library file (e.g. an installed copy); default in-tree
+LIB_PATH = Path(os.environ["FMS_LIBRARY"]) if os.environ.get("FMS_LIBRARY") else \
+    PKG / "libflashmaxsim_sm100.so"
 HEADER = PKG.parent / "include" / "fms.h"
 
 F32, F16, BF16, F64 = 0, 1, 2, 3

@@ -9,27 +9,31 @@
 // MAXMT tiles), document tokens on N (chunks of NT).  Each epilogue thread owns
 // one query-token row of the accumulator, so the per-token max over document
 // tokens is a register loop over TMEM columns -- no cross-thread reduction.
-// For queries of <= 32 tokens the 64-row tile holds the query twice (R = 2):
-// the MMA cost is the same, and the two copies let all four TMEM subpartitions
-// (all four epilogue warps) work, each on half of the chunk's columns.
+// For queries of <= 32 tokens a 128-row tile holds the query four times (R = 4):
+// every TMEM subpartition (every epilogue warp) then holds all 32 rows and takes
+// a quarter of the chunk's columns; the four partial (max, argmax) states meet
+// in shared memory.  With 256-column chunks a whole document is one MMA chain
+// (per-instruction issue cost, not tensor throughput, bounds small MMAs).
 //
-// Persistent CTAs walk the units (one query run x one document run); a unit may
+// Persistent CTAs walk contiguous ranges of units (one query run x one document
+// run; the query tile then changes rarely along a CTA's range); a unit may
 // stack several queries (in-batch, multi-query packed) so one document tile
 // feeds all of them.  Warp roles (224 threads):
 //   warp 6  scheduler: decodes 32 upcoming units at once (one per lane: candidate
 //           index, CSR bounds, first / last valid document token, document and
 //           query mask bits) into a 16-entry shared-memory metadata ring, so the
 //           dependent index -> mask global loads are off the other roles' paths;
-//   warp 0  TMA producer: per (chunk, 64-wide K block) loads the query tile(s)
-//           and the document rows of the chunk (64- and 16-row boxes, stopping at
-//           the last valid token, so masked padding is not read) into an S-stage
-//           ring;
+//   warp 0  TMA producer: loads the document rows of a chunk (128/64/32/16-row
+//           boxes, stopping at the last valid token, so masked padding is not
+//           read) into an S-stage ring, with the query tile either resident
+//           (re-loaded only when the unit's query changes) or carried per stage;
 //   warp 1  MMA issuer (one elected lane): 4 K=16 MMAs per K block into one of
-//           two TMEM accumulator buffers, tcgen05.commit to the ring slot and,
+//           NACC TMEM accumulator buffers, tcgen05.commit to the ring slot and,
 //           after the chunk's last K block, to the accumulator barrier;
 //   warps 2-5  epilogue: tcgen05.ld 32 columns at a time, masked running
-//           (max, argmax) per row, then Sigma_t per query in t order, the
-//           normalisation and the `neg` fill; every output written once.
+//           (max, argmax) per row -- a plain max when no tape is wanted -- then
+//           Sigma_t per query in t order, the normalisation and the `neg` fill;
+//           every output written once.
 // Every wait is bounded: on a timeout the CTA raises an error flag, stops
 // issuing, lets in-flight copies land, frees TMEM and returns.
 #include <cuda.h>
@@ -91,8 +95,10 @@ __device__ __forceinline__ TcUnit tc_decode(const TcParams& P, int64_t v) {
   const ScanParams& p = P.p;
   TcUnit U;
   if (p.layout == L_INBATCH || p.layout == L_PACKED) {
-    const int g = (int)(v % P.ngroups);
-    const int64_t j = v / P.ngroups;  // document: in-batch j, packed b
+    // query-group major: consecutive units share their query tile
+    const int64_t ndocs = (p.layout == L_INBATCH) ? p.Bd : p.B;
+    const int g = (int)(v / ndocs);
+    const int64_t j = v - (int64_t)g * ndocs;  // document: in-batch j, packed b
     const int qi0 = g * P.G;
     const int nqt = (p.layout == L_INBATCH) ? p.Bq : p.nq;
     U.valid = true;
@@ -180,80 +186,91 @@ __device__ __forceinline__ void mask_bits(const uint8_t* m, int n, uint32_t (&w)
 }
 
 
-// Shared-memory plan of one engine configuration.  ARES: the query tile of a unit
-// (all K blocks) stays resident in one of two slots and is re-loaded only when
-// the next unit's query differs; the S-stage ring then carries document rows
-// only.  Without ARES (large dim) every stage carries its K block of both.
-template <int M, int NT, int MAXMT, int S, int R, bool ARES>
+// Shared-memory / TMEM plan of one engine configuration.
+//  NT     document rows per chunk (one MMA N), NACC accumulator buffers in TMEM
+//         (the MMA may run NACC chunks ahead of the epilogue).
+//  ARES   the query tile of a unit (all K blocks) stays resident in one of two
+//         slots, re-loaded only when the unit's query differs from the previous
+//         unit's; a ring stage then carries one chunk of document rows for all
+//         K blocks (one barrier round trip per chunk).  Without ARES (large dim)
+//         a stage carries one K block of both operands.
+//  SMAX   ring stages available (the launch uses as many as fit its budget).
+template <int M, int NT, int MAXMT, int R, int NACC, int SMAX, int ARES>
 struct Cfg {
   static constexpr int A_BYTES = MAXMT * M * ROWB;  // one K block of all M tiles
-  static constexpr int B_BYTES = NT * ROWB;         // one K block of the chunk
-  static constexpr int STAGE = (ARES ? 0 : A_BYTES) + B_BYTES;
+  static constexpr int B_BYTES = NT * ROWB;         // one K block of a chunk
   static constexpr int ACC_COLS = MAXMT * NT;       // TMEM columns per accumulator buffer
-  static constexpr int TMEM_COLS = 2 * ACC_COLS;    // double-buffered
+  static constexpr int TMEM_COLS = NACC * ACC_COLS;
   static constexpr int HALF = NT / R;               // columns per epilogue thread per chunk
-  static constexpr bool EARLY = MAXMT * HALF <= 64; // copy the whole chunk to registers first
-  static int dyn_bytes(int KB) { return (ARES ? 2 * KB * A_BYTES : 0) + S * STAGE + 1024; }
-  static_assert(R == 1 || (R == 2 && M == 64 && MAXMT == 1), "replication needs one 64-row tile");
+  static __host__ __device__ int stage_bytes(int KB) { return ARES ? KB * B_BYTES : A_BYTES + B_BYTES; }
+  static __host__ __device__ int aslot_bytes(int KB) { return ARES ? KB * A_BYTES : 0; }
+  static_assert(R == 1 || (R == 2 && M == 64 && MAXMT == 1) || (R == 4 && M == 128 && MAXMT == 1),
+                "replication: 2 copies of 32 rows in a 64-row tile, or 4 in a 128-row tile");
   static_assert(TMEM_COLS == 128 || TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM columns");
+  static_assert(HALF % 32 == 0, "epilogue reads 32-column groups");
 };
 
 struct BMaps {
   CUtensorMap b128, b64, b32, b16;  // document rows, boxes of 128 / 64 / 32 / 16 rows
 };
 
-// Document rows [row, row + nr) of one K block (nr a multiple of 16, <= 128)
-// with at most three boxes.
+// Document rows [row, row + nr) of one K block (nr a multiple of 16, <= NT):
+// 128-row boxes, then at most one box each of 64, 32 and 16 rows.
 __device__ __forceinline__ void load_doc_rows(unsigned char* sB, const BMaps& bm, int x, int64_t row,
                                               int nr, uint64_t* bar) {
   int r = 0;
-  if (nr == 128) {
-    ptx::tma_load_2d(sB, &bm.b128, x, (int)row, bar);
-    return;
-  }
+  for (; nr - r >= 128; r += 128) ptx::tma_load_2d(sB + r * ROWB, &bm.b128, x, (int)(row + r), bar);
   if (nr - r >= 64) { ptx::tma_load_2d(sB + r * ROWB, &bm.b64, x, (int)(row + r), bar); r += 64; }
   if (nr - r >= 32) { ptx::tma_load_2d(sB + r * ROWB, &bm.b32, x, (int)(row + r), bar); r += 32; }
   if (nr - r >= 16) { ptx::tma_load_2d(sB + r * ROWB, &bm.b16, x, (int)(row + r), bar); r += 16; }
 }
 
-template <int M, int NT, int MAXMT, int S, int R, bool ARES, bool ARGS>
+template <int M, int NT, int MAXMT, int R, int NACC, int SMAX, int ARES, bool ARGS>
 __global__ void __launch_bounds__(NTHREADS, 1)
-tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ BMaps bm, TcParams P) {
-  using L = Cfg<M, NT, MAXMT, S, R, ARES>;
+tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ BMaps bm, TcParams P,
+               int S) {
+  using L = Cfg<M, NT, MAXMT, R, NACC, SMAX, ARES>;
   extern __shared__ __align__(1024) unsigned char dsm[];
-  __shared__ __align__(8) uint64_t full_bar[S];
-  __shared__ __align__(8) uint64_t empty_bar[S];
+  __shared__ __align__(8) uint64_t full_bar[SMAX];
+  __shared__ __align__(8) uint64_t empty_bar[SMAX];
   __shared__ __align__(8) uint64_t afull_bar[2];
   __shared__ __align__(8) uint64_t aempty_bar[2];
-  __shared__ __align__(8) uint64_t accf_bar[2];
-  __shared__ __align__(8) uint64_t acce_bar[2];
+  __shared__ __align__(8) uint64_t accf_bar[NACC];
+  __shared__ __align__(8) uint64_t acce_bar[NACC];
   __shared__ __align__(8) uint64_t metaf_bar[UQ];
   __shared__ __align__(8) uint64_t metae_bar[UQ];
-  __shared__ __align__(8) uint64_t epi_bar;  // epilogue-wide barrier (bounded, unlike bar.sync)
+  __shared__ __align__(8) uint64_t epi_bar;  // epilogue-wide barrier (bounded, unlike bar.sync);
+                                             // one arrival per epilogue warp
   __shared__ UnitMeta meta[UQ];
   __shared__ uint32_t tmem_base_s;
   __shared__ volatile int abort_s;
-  __shared__ float red_s[MAXMT * M];
-  __shared__ float half_mx[32];
-  __shared__ int half_ag[32];
-  __shared__ float half_s0[32];
+  // per-row results and the copies' states, double-buffered by unit parity so that
+  // the next unit may write while the current one is still being read
+  __shared__ __align__(16) float red_s[2][MAXMT * M];
+  __shared__ float half_mx[2][3][32];  // states of the copies 1..R-1, handed to copy 0
+  __shared__ int half_ag[2][3][32];
+  __shared__ float half_s0[2][3][32];
 
   unsigned char* tiles = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(dsm) + 1023) & ~(uintptr_t)1023);
-  unsigned char* aslots = tiles;                                          // ARES only
-  unsigned char* ring = tiles + (ARES ? 2 * P.KB * L::A_BYTES : 0);
+  unsigned char* aslots = tiles;  // ARES only
+  const int abytes = L::aslot_bytes(P.KB);
+  const int sbytes = L::stage_bytes(P.KB);
+  unsigned char* ring = tiles + ARES * abytes;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const ScanParams& p = P.p;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < S; ++i) {
+    for (int i = 0; i < SMAX; ++i) {
       ptx::mbar_init(&full_bar[i], 1);
       ptx::mbar_init(&empty_bar[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       ptx::mbar_init(&afull_bar[i], 1);
       ptx::mbar_init(&aempty_bar[i], 1);
+    }
+    for (int i = 0; i < NACC; ++i) {
       ptx::mbar_init(&accf_bar[i], 1);
       ptx::mbar_init(&acce_bar[i], 4);  // one arrival per epilogue warp
     }
@@ -261,7 +278,7 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       ptx::mbar_init(&metaf_bar[i], 1);
       ptx::mbar_init(&metae_bar[i], 6);  // producer + MMA + 4 epilogue warps
     }
-    ptx::mbar_init(&epi_bar, 128);
+    ptx::mbar_init(&epi_bar, 4);
     abort_s = 0;
     ptx::fence_barrier_init();
   }
@@ -277,7 +294,12 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem_base = tmem_base_s;
-  const int64_t my_units = P.nunits > blockIdx.x ? (P.nunits - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  // a contiguous range of units per CTA (query tiles change rarely along it)
+  const int64_t u_begin = P.nunits * blockIdx.x / gridDim.x;
+  const int64_t my_units = P.nunits * (blockIdx.x + 1) / gridDim.x - u_begin;
+  // K blocks per ring stage and stages per chunk
+  const int kbs = ARES ? P.KB : 1;
+  const int spc = ARES ? 1 : P.KB;
 
   if (warp == SCHED_WARP) {
     // ------------------------------------------------------------ scheduler
@@ -289,7 +311,7 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       UnitMeta m;
       int working = 0;
       if (i < my_units) {
-        const TcUnit U = tc_decode(P, blockIdx.x + i * gridDim.x);
+        const TcUnit U = tc_decode(P, u_begin + i);
         m.q_row0 = U.q_row0; m.d_row0 = U.d_row0;
         m.out0 = U.out0; m.out_stride = U.out_stride;
         m.arg0 = U.arg0; m.arg_stride = U.arg_stride;
@@ -353,7 +375,7 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     // ------------------------------------------------------------ TMA producer
     int stage = 0;
     uint32_t phase = 0;
-    int aslot = 1;           // ARES: slot of the current query tile
+    int aslot = ARES - 1;    // ARES: slot of the current query tile
     uint32_t aphase = 1;     // flips when aslot wraps to 0
     for (int64_t i = 0; i < my_units; ++i) {
       const int slot = (int)(i % UQ);
@@ -368,17 +390,16 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(&metae_bar[slot]);
       if (ARES && anew) {
-        aslot ^= 1;
-        if (aslot == 0) aphase ^= 1;
+        if (++aslot == ARES) { aslot = 0; aphase ^= 1; }
         if (!ptx::warp_wait(&aempty_bar[aslot], aphase ^ 1, &abort_s)) goto done;
         if (lane == 0) {
-          unsigned char* sA = aslots + aslot * P.KB * L::A_BYTES;
+          unsigned char* sA = aslots + aslot * abytes;
           ptx::mbar_expect_tx(&afull_bar[aslot], (uint32_t)(P.KB * nmt * M * ROWB));
           for (int kb = 0; kb < P.KB; ++kb) {
             unsigned char* sAk = sA + kb * L::A_BYTES;
-            if (R == 2) {  // the query twice: rows 0-31 and 32-63
-              ptx::tma_load_2d(sAk, &tmA, kb * KBLK, (int)q_row0, &afull_bar[aslot]);
-              ptx::tma_load_2d(sAk + 32 * ROWB, &tmA, kb * KBLK, (int)q_row0, &afull_bar[aslot]);
+            if (R > 1) {  // R copies of the 32-row query: rows 0-31, 32-63, ...
+              for (int q = 0; q < R; ++q)
+                ptx::tma_load_2d(sAk + q * 32 * ROWB, &tmA, kb * KBLK, (int)q_row0, &afull_bar[aslot]);
             } else {
               for (int mt = 0; mt < nmt; ++mt)
                 ptx::tma_load_2d(sAk + mt * M * ROWB, &tmA, kb * KBLK, (int)(q_row0 + mt * M),
@@ -392,23 +413,26 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const int u0 = c * NT;
         const int n = min(NT, leff - u0);
         const int nr = (n + 15) & ~15;
-        for (int kb = 0; kb < P.KB; ++kb) {
+        for (int ks = 0; ks < spc; ++ks) {
           if (!ptx::warp_wait(&empty_bar[stage], phase ^ 1, &abort_s)) goto done;
           if (lane == 0) {
-            unsigned char* st = ring + stage * L::STAGE;
-            unsigned char* sB = st + (ARES ? 0 : L::A_BYTES);
-            ptx::mbar_expect_tx(&full_bar[stage], (uint32_t)((ARES ? 0 : nmt * M * ROWB) + nr * ROWB));
-            if (!ARES) {
-              if (R == 2) {
-                ptx::tma_load_2d(st, &tmA, kb * KBLK, (int)q_row0, &full_bar[stage]);
-                ptx::tma_load_2d(st + 32 * ROWB, &tmA, kb * KBLK, (int)q_row0, &full_bar[stage]);
+            unsigned char* st = ring + stage * sbytes;
+            if (ARES) {
+              ptx::mbar_expect_tx(&full_bar[stage], (uint32_t)(kbs * nr * ROWB));
+              for (int kb = 0; kb < kbs; ++kb)
+                load_doc_rows(st + kb * L::B_BYTES, bm, kb * KBLK, d_row0 + u0, nr, &full_bar[stage]);
+            } else {
+              ptx::mbar_expect_tx(&full_bar[stage], (uint32_t)(nmt * M * ROWB + nr * ROWB));
+              if (R > 1) {
+                for (int q = 0; q < R; ++q)
+                  ptx::tma_load_2d(st + q * 32 * ROWB, &tmA, ks * KBLK, (int)q_row0, &full_bar[stage]);
               } else {
                 for (int mt = 0; mt < nmt; ++mt)
-                  ptx::tma_load_2d(st + mt * M * ROWB, &tmA, kb * KBLK, (int)(q_row0 + mt * M),
+                  ptx::tma_load_2d(st + mt * M * ROWB, &tmA, ks * KBLK, (int)(q_row0 + mt * M),
                                    &full_bar[stage]);
               }
+              load_doc_rows(st + L::A_BYTES, bm, ks * KBLK, d_row0 + u0, nr, &full_bar[stage]);
             }
-            load_doc_rows(sB, bm, kb * KBLK, d_row0 + u0, nr, &full_bar[stage]);
           }
           __syncwarp();
           if (++stage == S) { stage = 0; phase ^= 1; }
@@ -421,7 +445,7 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     uint32_t phase = 0;
     int as = 0;
     uint32_t aphase = 0;
-    int aslot = 1;
+    int aslot = ARES - 1;
     uint32_t aslot_phase = 1;
     bool holding = false;    // ARES: an A slot is in use (released on the next switch)
     for (int64_t i = 0; i < my_units; ++i) {
@@ -437,8 +461,7 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       if (lane == 0) ptx::mbar_arrive(&metae_bar[slot]);
       if (ARES && anew) {
         if (holding && lane == 0) ptx::mma_commit(&aempty_bar[aslot]);  // after its last MMA
-        aslot ^= 1;
-        if (aslot == 0) aslot_phase ^= 1;
+        if (++aslot == ARES) { aslot = 0; aslot_phase ^= 1; }
         if (!ptx::warp_wait(&afull_bar[aslot], aslot_phase, &abort_s)) goto done;
         ptx::tc_fence_after();
         holding = true;
@@ -449,20 +472,23 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const uint32_t idesc = ptx::idesc_f16(P.fmt, M, nr);
         if (!ptx::warp_wait(&acce_bar[as], aphase ^ 1, &abort_s)) goto done;
         ptx::tc_fence_after();
-        for (int kb = 0; kb < P.KB; ++kb) {
+        for (int ks = 0; ks < spc; ++ks) {
           if (!ptx::warp_wait(&full_bar[stage], phase, &abort_s)) goto done;
           ptx::tc_fence_after();
           if (lane == 0) {
-            const uint32_t st = ptx::smem_u32(ring + stage * L::STAGE);
-            const uint32_t sA = ARES ? ptx::smem_u32(aslots + (aslot * P.KB + kb) * L::A_BYTES) : st;
-            const uint32_t sB = st + (ARES ? 0 : L::A_BYTES);
-            const uint64_t bdesc = ptx::sw128_desc(sB);
-            for (int mt = 0; mt < nmt; ++mt) {
-              const uint64_t adesc = ptx::sw128_desc(sA + mt * M * ROWB);
-              const uint32_t d = tmem_base + (uint32_t)(as * L::ACC_COLS + mt * NT);
+            const uint32_t st = ptx::smem_u32(ring + stage * sbytes);
+            for (int kk = 0; kk < kbs; ++kk) {
+              const int kb = ARES ? kk : ks;
+              const uint32_t sA = ARES ? ptx::smem_u32(aslots + aslot * abytes + kb * L::A_BYTES) : st;
+              const uint32_t sB = ARES ? st + kk * L::B_BYTES : st + L::A_BYTES;
+              const uint64_t bdesc = ptx::sw128_desc(sB);
+              for (int mt = 0; mt < nmt; ++mt) {
+                const uint64_t adesc = ptx::sw128_desc(sA + mt * M * ROWB);
+                const uint32_t d = tmem_base + (uint32_t)(as * L::ACC_COLS + mt * NT);
 #pragma unroll
-              for (int k = 0; k < KBLK / 16; ++k)
-                ptx::mma_f16(d, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0);
+                for (int k = 0; k < KBLK / 16; ++k)
+                  ptx::mma_f16(d, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0);
+              }
             }
             ptx::mma_commit(&empty_bar[stage]);
           }
@@ -471,8 +497,7 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         }
         if (lane == 0) ptx::mma_commit(&accf_bar[as]);
         __syncwarp();
-        as ^= 1;
-        if (as == 0) aphase ^= 1;
+        if (++as == NACC) { as = 0; aphase ^= 1; }
       }
     }
   } else {
@@ -480,9 +505,12 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     const int sp = warp & 3;   // TMEM subpartition of this warp
     const int et = threadIdx.x - 64;  // 0..127
     // row of the accumulator this thread reads, and its column half
-    const int lr = (M == 128) ? sp * 32 + lane
-                              : (lane < 16 ? (R == 2 ? (sp & 1) * 16 : sp * 16) + lane : -1);
-    const int h = (R == 2) ? (sp >> 1) : 0;
+    //  R = 4: every subpartition holds rows 0-31 (one copy each) -> column quarter sp
+    //  R = 2: subpartitions {0,1} and {2,3} hold the two copies -> column half sp/2
+    const int lr = (R == 4) ? lane
+                 : (M == 128) ? sp * 32 + lane
+                 : (lane < 16 ? (R == 2 ? (sp & 1) * 16 : sp * 16) + lane : -1);
+    const int h = (R == 4) ? sp : (R == 2) ? (sp >> 1) : 0;
     int as = 0;
     uint32_t aphase = 0;
     uint32_t ephase = 0;
@@ -491,6 +519,7 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       const int slot = (int)(i % UQ);
       if (!ptx::warp_wait(&metaf_bar[slot], (uint32_t)((i / UQ) & 1), &abort_s)) goto done;
       const UnitMeta& m = meta[slot];
+      const int ub = (int)(i & 1);  // buffer of this unit (red_s, half_*)
       if (!m.valid) {
         if (et == 0) scores[m.out0] = (float)p.neg;
         if (ARGS)
@@ -531,56 +560,18 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const uint32_t tb = tmem_base + ((uint32_t)(sp * 32) << 16) + (uint32_t)(as * L::ACC_COLS);
         const int fc = first - u0 - h * L::HALF;  // first valid column, in my half?
         const bool s0_here = fc >= 0 && fc < L::HALF && first - u0 < n;
-        if (L::EARLY) {
-          // copy the chunk to registers and hand the accumulator back at once
-          uint32_t r[MAXMT][L::HALF / 32][32];
-          uint32_t r0[MAXMT];
 #pragma unroll
-          for (int mt = 0; mt < MAXMT; ++mt) {
-            if (mt < nmt) {
+        for (int mt = 0; mt < MAXMT; ++mt) {
+          if (mt < nmt) {
 #pragma unroll
-              for (int g = 0; g < L::HALF / 32; ++g)
-                if (h * L::HALF + 32 * g < n) ptx::tmem_ld32(tb + mt * NT + h * L::HALF + 32 * g, r[mt][g]);
-              if (s0_here) r0[mt] = ptx::tmem_ld1(tb + mt * NT + (first - u0));
-            }
-          }
-          ptx::tmem_wait_ld();
-          ptx::tc_fence_before();
-          __syncwarp();
-          if (lane == 0) ptx::mbar_arrive(&acce_bar[as]);
-#pragma unroll
-          for (int mt = 0; mt < MAXMT; ++mt) {
-            if (mt < nmt) {
-#pragma unroll
-              for (int g = 0; g < L::HALF / 32; ++g) {
-                const int col0 = h * L::HALF + 32 * g;
-                if (col0 < n) {
-                  const uint32_t mm = mw[g];
-#pragma unroll
-                  for (int cc = 0; cc < 32; ++cc) {
-                    const float s = __uint_as_float(r[mt][g][cc]);
-                    if (((mm >> cc) & 1u) && s > mx[mt]) {
-                      mx[mt] = s;
-                      ag[mt] = u0 + col0 + cc + 1;
-                    }
-                  }
-                }
-              }
-              if (s0_here) { s0[mt] = __uint_as_float(r0[mt]); has_s0 = true; }
-            }
-          }
-        } else {
-#pragma unroll
-          for (int mt = 0; mt < MAXMT; ++mt) {
-            if (mt < nmt) {
-#pragma unroll
-              for (int g = 0; g < L::HALF / 32; ++g) {
-                const int col0 = h * L::HALF + 32 * g;
-                if (col0 < n) {
-                  uint32_t r[32];
-                  ptx::tmem_ld32(tb + mt * NT + col0, r);
-                  ptx::tmem_wait_ld();
-                  const uint32_t mm = mw[g];
+            for (int g = 0; g < L::HALF / 32; ++g) {
+              const int col0 = h * L::HALF + 32 * g;
+              if (col0 < n) {
+                uint32_t r[32];
+                ptx::tmem_ld32(tb + mt * NT + col0, r);
+                ptx::tmem_wait_ld();
+                const uint32_t mm = mw[g];
+                if (ARGS) {
 #pragma unroll
                   for (int cc = 0; cc < 32; ++cc) {
                     const float s = __uint_as_float(r[cc]);
@@ -589,35 +580,51 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                       ag[mt] = u0 + col0 + cc + 1;
                     }
                   }
+                } else if (mm == 0xffffffffu) {
+                  // values only: max of the non-NaN entries (what strict `>` from
+                  // -inf keeps); the first-valid rule is applied at the end
+#pragma unroll
+                  for (int cc = 0; cc < 32; ++cc) mx[mt] = fmaxf(mx[mt], __uint_as_float(r[cc]));
+                } else {
+#pragma unroll
+                  for (int cc = 0; cc < 32; ++cc)
+                    mx[mt] = fmaxf(mx[mt], ((mm >> cc) & 1u) ? __uint_as_float(r[cc]) : -INFINITY);
                 }
               }
-              if (s0_here) {
-                s0[mt] = __uint_as_float(ptx::tmem_ld1(tb + mt * NT + (first - u0)));
-                ptx::tmem_wait_ld();
-                has_s0 = true;
-              }
+            }
+            if (s0_here) {
+              s0[mt] = __uint_as_float(ptx::tmem_ld1(tb + mt * NT + (first - u0)));
+              ptx::tmem_wait_ld();
+              has_s0 = true;
             }
           }
-          ptx::tc_fence_before();
-          __syncwarp();
-          if (lane == 0) ptx::mbar_arrive(&acce_bar[as]);
         }
-        as ^= 1;
-        if (as == 0) aphase ^= 1;
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&acce_bar[as]);
+        if (++as == NACC) { as = 0; aphase ^= 1; }
       }
-      if (R == 2) {
-        // the second copy of rows 0-31 (columns of the upper half) hands its state over
-        if (h == 1 && lr >= 0) {
-          half_mx[lr] = mx[0];
-          half_ag[lr] = ag[0];
-          half_s0[lr] = has_s0 ? s0[0] : __int_as_float(0x7fc00001);
+      if (R > 1) {
+        // copies 1..R-1 of rows 0-31 (the other column slices) hand their states over
+        if (h > 0 && lr >= 0) {
+          half_mx[ub][h - 1][lr] = mx[0];
+          half_ag[ub][h - 1][lr] = ag[0] | (has_s0 ? (1 << 30) : 0);  // flag: this slice read column `first`
+          half_s0[ub][h - 1][lr] = has_s0 ? s0[0] : 0.f;
         }
-        ptx::mbar_arrive(&epi_bar);
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&epi_bar);
         if (!ptx::warp_wait(&epi_bar, ephase, &abort_s)) goto done;
         ephase ^= 1;
         if (h == 0 && lr >= 0) {
-          merge_state(mx[0], ag[0], half_mx[lr], half_ag[lr]);
-          if (!has_s0) s0[0] = half_s0[lr];
+#pragma unroll
+          for (int q = 0; q < R - 1; ++q) {
+            const int a2 = half_ag[ub][q][lr];
+            if (ARGS)
+              merge_state(mx[0], ag[0], half_mx[ub][q][lr], a2 & ~(1 << 30));
+            else
+              mx[0] = fmaxf(mx[0], half_mx[ub][q][lr]);
+            if (!has_s0 && (a2 & (1 << 30))) { s0[0] = half_s0[ub][q][lr]; has_s0 = true; }
+          }
         }
       }
       // finish the rows: exact first-valid rule, tape, per-row contribution
@@ -629,23 +636,43 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           const bool tv = (m.qw[r >> 5] >> (r & 31)) & 1u;
           float v = mx[mt];
           int a = ag[mt];
-          final_fixup(v, a, first, s0[mt]);
-          const bool ok = tv && a > 0;
-          red_s[r] = ok ? v : 0.f;
+          bool ok;
+          if (ARGS) {
+            final_fixup(v, a, first, s0[mt]);
+            ok = tv && a > 0;
+          } else {
+            // a NaN in the first valid column sticks; otherwise the max of the
+            // non-NaN values (>= that column's value) is the result
+            if (first >= 0 && s0[mt] != s0[mt]) v = s0[mt];
+            ok = tv && first >= 0;
+          }
+          red_s[ub][r] = ok ? v : 0.f;
           if (ARGS) p.args[m.arg0 + qi * m.arg_stride + t] = ok ? a : 0;
         }
       }
-      ptx::mbar_arrive(&epi_bar);
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&epi_bar);
       if (!ptx::warp_wait(&epi_bar, ephase, &abort_s)) goto done;
       ephase ^= 1;
       if (et < m.nq) {
         const int qi = et;
+        const float* rs = red_s[ub] + qi * m.Tq;
         float score = 0.f;
         int nvalid = 0;
-#pragma unroll 8
-        for (int t = 0; t < m.Tq; ++t) {  // Sigma_t in t order (forward_pair.jl:92-95)
+        // Sigma_t in t order (forward_pair.jl:92-95)
+        if ((m.Tq & 3) == 0) {
+          for (int t = 0; t < m.Tq; t += 4) {
+            const float4 v4 = *reinterpret_cast<const float4*>(rs + t);
+            score += v4.x;
+            score += v4.y;
+            score += v4.z;
+            score += v4.w;
+          }
+        } else {
+          for (int t = 0; t < m.Tq; ++t) score += rs[t];
+        }
+        for (int t = 0; t < m.Tq; ++t) {
           const int r = qi * m.Tq + t;
-          score += red_s[r];
           nvalid += (m.qw[r >> 5] >> (r & 31)) & 1u;
         }
         if (p.normalize) score = score * (1.0f / (float)(nvalid > 1 ? nvalid : 1));
@@ -655,9 +682,6 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         for (int t = m.Tq + et; t < m.arg_rows; t += 128) p.args[m.arg0 + t] = 0;
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(&metae_bar[slot]);
-      ptx::mbar_arrive(&epi_bar);  // red_s / half_* are reused by the next unit
-      if (!ptx::warp_wait(&epi_bar, ephase, &abort_s)) goto done;
-      ephase ^= 1;
     }
   }
 done:
@@ -728,27 +752,42 @@ static void plan(const ScanParams& p, int& G, int& rows) {
   rows = G * Tq;
 }
 
-template <int M, int NT, int MAXMT, int S, int R, bool ARES>
+// Launch one configuration.  budget: dynamic shared memory per CTA (bytes) for
+// the query slots and the ring; ctas_per_sm: CTAs that share an SM (TMEM is
+// sized for it; every configuration stays at or under 128 registers per thread,
+// the per-SMSP limit for two 7-warp CTAs).
+template <int M, int NT, int MAXMT, int R, int NACC, int SMAX, int ARES>
 static cudaError_t launch_cfg(const TcParams& P, const CUtensorMap& a, const BMaps& bm, cudaStream_t s,
-                              int ctas_per_sm) {
-  using L = Cfg<M, NT, MAXMT, S, R, ARES>;
+                              int ctas_per_sm, int budget) {
+  using L = Cfg<M, NT, MAXMT, R, NACC, SMAX, ARES>;
+  const int sb = L::stage_bytes(P.KB);
+  int S = (budget - ARES * L::aslot_bytes(P.KB)) / sb;
+  if (S > SMAX) S = SMAX;
+  if (S < 2) return cudaErrorNotSupported;
+  const int dyn = ARES * L::aslot_bytes(P.KB) + S * sb + 1024;
+  auto k = P.p.args ? tc_scan_kernel<M, NT, MAXMT, R, NACC, SMAX, ARES, true>
+                    : tc_scan_kernel<M, NT, MAXMT, R, NACC, SMAX, ARES, false>;
+  cudaError_t e;
+  if ((e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn)) != cudaSuccess)
+    return e;
   int64_t grid = (int64_t)device_sm_count() * ctas_per_sm;
   if (grid > P.nunits) grid = P.nunits;
   if (grid < 1) grid = 1;
-  const int dyn = L::dyn_bytes(P.KB);
-  cudaError_t e;
-  if (P.p.args) {
-    auto k = tc_scan_kernel<M, NT, MAXMT, S, R, ARES, true>;
-    if ((e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn)) != cudaSuccess)
-      return e;
-    k<<<(unsigned)grid, NTHREADS, dyn, s>>>(a, bm, P);
-  } else {
-    auto k = tc_scan_kernel<M, NT, MAXMT, S, R, ARES, false>;
-    if ((e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn)) != cudaSuccess)
-      return e;
-    k<<<(unsigned)grid, NTHREADS, dyn, s>>>(a, bm, P);
-  }
+  k<<<(unsigned)grid, NTHREADS, dyn, s>>>(a, bm, P, S);
   return cudaGetLastError();
+}
+
+// Resident query tiles: two slots (a new query loads while the previous one is
+// in use) when they leave room for three ring stages, else one slot and two
+// stages, else none (every stage carries its own query K block).
+template <int M, int NT, int MAXMT, int R, int NACC, int SMAX>
+static cudaError_t launch_auto(const TcParams& P, const CUtensorMap& a, const BMaps& bm, cudaStream_t s,
+                               int ctas_per_sm, int budget) {
+  using LA = Cfg<M, NT, MAXMT, R, NACC, SMAX, 1>;
+  const int ab = LA::aslot_bytes(P.KB), sb = LA::stage_bytes(P.KB);
+  if (2 * ab + 3 * sb <= budget) return launch_cfg<M, NT, MAXMT, R, NACC, SMAX, 2>(P, a, bm, s, ctas_per_sm, budget);
+  if (ab + 2 * sb <= budget) return launch_cfg<M, NT, MAXMT, R, NACC, SMAX, 1>(P, a, bm, s, ctas_per_sm, budget);
+  return launch_cfg<M, NT, MAXMT, R, NACC, SMAX, 0>(P, a, bm, s, ctas_per_sm, budget);
 }
 
 }  // namespace tc
@@ -806,23 +845,13 @@ cudaError_t launch_scan_tc(int dtype, const ScanParams& p, cudaStream_t s) {
       !tc::make_map(&bm.b32, p.D, P.fmt, p.dim, p.nd_tok, 32) ||
       !tc::make_map(&bm.b16, p.D, P.fmt, p.dim, p.nd_tok, 16))
     return cudaErrorNotSupported;
-  // The query tile stays resident when both slots fit next to the ring.
-  const bool small_k = P.KB <= 2;   // dim <= 128
-  const bool mid_k = P.KB <= 4;     // dim <= 256
-  if (rep) {
-    if (mid_k) return tc::launch_cfg<64, 128, 1, 4, 2, true>(P, a, bm, s, small_k ? 2 : 1);
-    return tc::launch_cfg<64, 128, 1, 4, 2, false>(P, a, bm, s, 2);
-  }
-  if (rows <= 64) {
-    if (mid_k) return tc::launch_cfg<64, 128, 1, 4, 1, true>(P, a, bm, s, small_k ? 2 : 1);
-    return tc::launch_cfg<64, 128, 1, 4, 1, false>(P, a, bm, s, 2);
-  }
-  if (rows <= 128) {
-    if (small_k) return tc::launch_cfg<128, 128, 1, 8, 1, true>(P, a, bm, s, 1);
-    return tc::launch_cfg<128, 128, 1, 3, 1, false>(P, a, bm, s, 2);
-  }
-  if (small_k) return tc::launch_cfg<128, 128, 2, 5, 1, true>(P, a, bm, s, 1);
-  return tc::launch_cfg<128, 128, 2, 4, 1, false>(P, a, bm, s, 1);
+  // Two CTAs per SM get ~100 KB of dynamic shared memory each, one CTA ~200 KB.
+  constexpr int B2 = 100 * 1024, B1 = 200 * 1024;
+  if (rep)  // one 32-row query, 4 copies in a 128-row tile: a whole document per MMA chain
+    return tc::launch_cfg<128, 256, 1, 4, 1, 2, 0>(P, a, bm, s, 2, B2);
+  if (rows <= 64) return tc::launch_auto<64, 64, 1, 1, 4, 8>(P, a, bm, s, 2, B2);
+  if (rows <= 128) return tc::launch_auto<128, 64, 1, 1, 4, 8>(P, a, bm, s, 2, B2);
+  return tc::launch_auto<128, 128, 2, 1, 2, 12>(P, a, bm, s, 1, B1);
 }
 
 }  // namespace fms

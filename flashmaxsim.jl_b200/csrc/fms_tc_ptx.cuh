@@ -51,16 +51,22 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Wait for the phase of `bar` with the given parity.  Gives up (returns false)
 // when *abort is raised by another role or after `limit_ns`, raising *abort.
+// The abort flag and the clock are consulted every 256 polls only, so a wait
+// that ends soon costs nothing but the polls.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
                                           uint64_t limit_ns = 2000000000ull) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
-  while (true) {
+  uint64_t t0 = 0;
+  for (uint32_t it = 0;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (*abort) return false;
-    if (globaltimer_ns() - t0 > limit_ns) {
-      *abort = 1;
-      return false;
+    if ((it & 255u) == 255u) {
+      if (*abort) return false;
+      const uint64_t now = globaltimer_ns();
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > limit_ns) {
+        *abort = 1;
+        return false;
+      }
     }
   }
 }
