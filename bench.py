@@ -158,6 +158,29 @@ class ClockSampler:
                 "samples": len(sm), "reasons": sorted(reasons)}
 
 
+def arm_config(world, total_tok):
+    """The workload both arms report (ours and the reference CPU arm)."""
+    return {"workload": "c2 candidate rerank fp16: 64 q x 32 tok x 128 dim, gallery "
+                        f"{NDOC * world} docs x 256 tok (valid U[64,256]), idxs "
+                        f"{C * world}x64 (2% invalid, neg=-Inf)",
+            "gallery_per_gpu": NDOC, "doc_tokens_per_step": total_tok,
+            "l2": "inputs larger than L2 (2.6 GB of gallery read per step)",
+            "parallelism": f"gallery sharded by doc id over {world} GPU(s)" +
+                           (", NCCL all-reduce(max) merge" if world > 1 else "")}
+
+
+def profiled_traffic():
+    """DRAM bytes per scan launch (dram__bytes_read.sum + dram__bytes_write.sum)
+    from the committed ncu summary of the full-size c2 launch, or None."""
+    p = ROOT / "profiles" / "tc_scan_c2_dram.md"
+    if not p.exists():
+        return None, None
+    for line in p.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            return float(line.split(":", 1)[1].strip()), p.name
+    return None, None
+
+
 def measured_peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -184,16 +207,21 @@ def cpu_sample(Q, gallery, dmask, idxs, nq=8):
     return Qn, G, dm, ix_local, ntok
 
 
-def time_cpu(Qn, G, dm, ix, ntok, reps=1, threads=None):
+def time_cpu(Qn, G, dm, ix, ntok, min_seconds=10.0, threads=None):
+    """Repeat the CPU pass until at least `min_seconds` of CPU work was timed."""
     sys.path.insert(0, str(ROOT / "oracle"))
     import oracle as O
     threads = threads or O.default_threads()
     O.candidates(Qn[:1], G, ix[:1], None, dm, neg=float("-inf"), nthreads=threads)  # warm
     t0 = time.perf_counter()
-    for _ in range(reps):
+    reps = 0
+    while True:
         O.candidates(Qn, G, ix, None, dm, neg=float("-inf"), nthreads=threads)
+        reps += 1
+        if time.perf_counter() - t0 >= min_seconds:
+            break
     dt = (time.perf_counter() - t0) / reps
-    return ntok / dt, threads, dt
+    return ntok / dt, threads, dt, reps
 
 
 def run_reference(args, world, rank):
@@ -204,6 +232,7 @@ def run_reference(args, world, rank):
         print(json.dumps({"impl": "reference", "unavailable": "no device to build the workload"}))
         return
     Q, gallery, dmask, lens, idxs = make_workload(1, 0, dev)
+    full_tok, _ = doc_tokens(idxs, lens, 1, 0)
     Qn, G, dm, ix, ntok = cpu_sample(Q, gallery, dmask, idxs, nq=4)
     del gallery
     sys.path.insert(0, str(ROOT / "oracle"))
@@ -223,8 +252,7 @@ def run_reference(args, world, rank):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded randn, L2-normalised tokens)",
-        "config": {"workload": "c2 candidate rerank fp16: 64 q x 32 tok x 128, gallery 100k x 256, "
-                               "idxs 1000x64 (2% invalid); CPU sample of 4 queries"},
+        "config": arm_config(1, full_tok),
         "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -326,36 +354,32 @@ def main():
         idxs.numel() * 4
     peak, peak_kind = measured_peaks()
     achieved = alg_bytes / (ms_step / 1e3) / 1e9
+    traffic, traffic_src = profiled_traffic() if world == 1 else (None, None)
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f16",
         "data": "synthetic (seeded randn, L2-normalised tokens; no dataset in the reference)",
-        "config": {"workload": "c2 candidate rerank fp16: 64 q x 32 tok x 128 dim, gallery "
-                               f"{NDOC * world} docs x 256 tok (valid U[64,256]), idxs "
-                               f"{C * world}x64 (2% invalid, neg=-Inf)",
-                   "gallery_per_gpu": NDOC, "doc_tokens_per_step": total_tok,
-                   "l2": "inputs larger than L2 (2.6 GB of gallery read per step)",
-                   "parallelism": f"gallery sharded by doc id over {world} GPU(s)" +
-                                  (", NCCL all-reduce(max) merge" if world > 1 else "")},
+        "config": arm_config(world, total_tok),
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h,
                 "note": "gallery resident in HBM (index); queries+idxs H2D, scores D2H"},
         "gpu_launches": args.steps * (1 if world == 1 else 2),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "traffic": None,
+                     "frac": achieved / peak, "traffic": traffic,
+                     "traffic_source": traffic_src,
                      "peak_source": f"{peak_kind} hbm_gbs", "kernel": "candidates scan",
                      "algorithmic_bytes_per_launch": alg_bytes},
         "clocks": clk,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         Qn, G, dm, ix, ctok = cpu_sample(Q, gallery, dmask, idxs, nq=8)
-        v, thr, dt = time_cpu(Qn, G, dm, ix, ctok, reps=2)
+        v, thr, dt, reps = time_cpu(Qn, G, dm, ix, ctok, min_seconds=10.0)
         line["cpu_baseline"] = {
             "value": v, "unit": UNIT, "cores": thr, "kind": "port",
-            "sample": f"8 of 64 queries x all candidates ({ctok} valid doc-tokens, {dt:.2f} s "
-                      "per pass), oracle C port of the reference CPU Array path, OpenMP over "
-                      "pairs"}
+            "sample": f"8 of 64 queries x all candidates ({ctok} valid doc-tokens per pass, "
+                      f"{reps} passes, {dt * reps:.1f} s), oracle C port of the reference CPU "
+                      "Array path, OpenMP over pairs"}
     if rank == 0:
         print(json.dumps(line))
     if world > 1:
