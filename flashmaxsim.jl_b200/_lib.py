@@ -53,6 +53,8 @@ SIGNATURES = {
     "fms_pair_bwd": (_i, [_i, _i, _P, _P, _P, _P, _P, _i, _i, _i, _P, _P, _P, _sz, _P]),
     "fms_paired_bwd": (_i, [_i, _i, _P, _P, _P, _P, _P, _P, _i, _i, _i, _i, _P, _P, _P, _sz,
                             _P]),
+    "fms_paired_bwd_invgrid_noalloc": (_i, [_i, _P, _P, _P, _P, _P, _P, _i, _i, _i, _i, _P, _P,
+                                            _P]),
     "fms_inbatch_bwd": (_i, [_i, _i, _P, _P, _P, _P, _P, _P, _i, _i, _i, _i, _i, _P, _P, _P,
                              _sz, _P]),
     "fms_candidates_bwd": (_i, [_i, _i, _P, _P, _P, _P, _P, _P, _P, _i, _i, _i, _i, _i64, _i,

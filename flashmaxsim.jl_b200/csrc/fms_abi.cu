@@ -88,6 +88,7 @@ const char* fms_status_string(int status) {
     case FMS_ERR_ALIGN: return "pointer alignment requirement not met";
     case FMS_ERR_WORKSPACE: return "workspace missing or too small";
     case FMS_ERR_UNSUPPORTED: return "unsupported device or feature";
+    case FMS_ERR_TOO_LARGE: return "input too large for the fixed scratch of a no-allocation entry point";
     default: return status > 0 ? cudaGetErrorString((cudaError_t)status) : "unknown error";
   }
 }
@@ -263,6 +264,55 @@ int fms_paired_bwd(int dtype, int strategy, const void* Delta, const void* inv_n
   b.Delta = Delta; b.inv_n = inv_n; b.dQ = dQ; b.dD = dD;
   b.nq_rows = (int64_t)Tq * B; b.nd_rows = (int64_t)Td * B;
   return run_bwd(dtype, strategy, b, workspace, ws_bytes, (cudaStream_t)stream);
+}
+
+// ---------------------------------------------------------------------------
+// No-allocation variant of the InvGrid paired backward.  Its CSR scratch lives in
+// a fixed device array of this library instead of a caller workspace.
+//
+// FMS_STATIC_SCRATCH_BYTES (4 MiB) bounds the problem: the InvGrid CSR needs
+// about 4 * (2 * B*Td + B*Tq) bytes plus alignment, i.e. up to roughly 340 k
+// document tokens for Tq = 32 sources per 180-token document.
+static __device__ __align__(256) unsigned char g_static_scratch[FMS_STATIC_SCRATCH_BYTES];
+
+static void* g_scratch_addr[64];
+static std::mutex g_scratch_mu;
+
+// Device address of the scratch on the current device, looked up once per
+// device (cudaGetSymbolAddress) and cached.
+static cudaError_t static_scratch(void** out) {
+  int d = 0;
+  cudaError_t e = cudaGetDevice(&d);
+  if (e != cudaSuccess) return e;
+  if (d < 0 || d >= 64) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (g_scratch_addr[d] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_static_scratch);
+    if (e != cudaSuccess) return e;
+    g_scratch_addr[d] = p;
+  }
+  *out = g_scratch_addr[d];
+  return cudaSuccess;
+}
+
+int fms_paired_bwd_invgrid_noalloc(int dtype, const void* Delta, const void* inv_n, const void* Q,
+                                   const void* D, const uint8_t* qmask, const int32_t* args,
+                                   int dim, int Tq, int Td, int B, void* dQ, void* dD,
+                                   fms_stream_t stream) {
+  if (dim < 0 || Tq < 0 || Td < 0 || B < 0) return FMS_ERR_INVALID;
+  if (!dtype_ok(dtype)) return FMS_ERR_DTYPE;
+  const int64_t n_src = (int64_t)Tq * B, n_dest = (int64_t)Td * B;
+  if (bwd_workspace_bytes(FMS_INVGRID, dtype, n_src, n_dest, n_dest * dim) >
+      (size_t)FMS_STATIC_SCRATCH_BYTES)
+    return FMS_ERR_TOO_LARGE;
+  void* ws = nullptr;
+  cudaError_t e = static_scratch(&ws);
+  if (e != cudaSuccess) return (int)e;
+  // everything of the scratch that must start at zero (the CSR row counts) is
+  // cleared on the stream by the InvGrid path itself before use
+  return fms_paired_bwd(dtype, FMS_INVGRID, Delta, inv_n, Q, D, qmask, args, dim, Tq, Td, B, dQ,
+                        dD, ws, (size_t)FMS_STATIC_SCRATCH_BYTES, stream);
 }
 
 int fms_inbatch_bwd(int dtype, int strategy, const void* Delta, const void* inv_n, const void* Q,

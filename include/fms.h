@@ -51,6 +51,10 @@ enum fms_backward { FMS_ATOMIC_UNIFIED = 0, FMS_INVGRID = 1 };
 #define FMS_ERR_ALIGN (-3)       /* pointer alignment not met */
 #define FMS_ERR_WORKSPACE (-4)   /* workspace missing or too small */
 #define FMS_ERR_UNSUPPORTED (-5) /* no sm_100 device, or feature unavailable */
+#define FMS_ERR_TOO_LARGE (-6)   /* input exceeds a no-allocation entry point's scratch */
+
+/* Fixed device scratch of fms_paired_bwd_invgrid_noalloc (bytes). */
+#define FMS_STATIC_SCRATCH_BYTES (4u << 20)
 
 /* Human-readable text for a status code (static storage). */
 const char* fms_status_string(int status);
@@ -154,6 +158,26 @@ int fms_paired_bwd(int dtype, int strategy, const void* Delta, const void* inv_n
                    const void* Q, const void* D, const uint8_t* qmask, const int32_t* args,
                    int dim, int Tq, int Td, int B, void* dQ, void* dD, void* workspace,
                    size_t ws_bytes, fms_stream_t stream);
+
+/* No counterpart in the reference: fms_paired_bwd with FMS_INVGRID for callers
+   that cannot pass a workspace and must not allocate device memory on the call
+   path (cudaMalloc / cudaFree synchronise the device and can fail under memory
+   pressure, which a latency-bound serving loop or a caller holding only a
+   fixed memory budget cannot afford).  The CSR scratch is a fixed array of
+   FMS_STATIC_SCRATCH_BYTES inside this library; the call allocates nothing.
+   - Inputs whose InvGrid scratch (fms_bwd_workspace_size(FMS_INVGRID, ...))
+     exceeds FMS_STATIC_SCRATCH_BYTES return FMS_ERR_TOO_LARGE before any work.
+   - The scratch address is looked up once per device (cudaGetSymbolAddress) on
+     the first call on that device; make that first call before any stream
+     capture begins.
+   - One scratch per device: calls that overlap in time on the same device (other
+     streams, other host threads) race on it and corrupt each other's results.
+     Serialise them.
+   Results are identical to fms_paired_bwd(dtype, FMS_INVGRID, ...). */
+int fms_paired_bwd_invgrid_noalloc(int dtype, const void* Delta, const void* inv_n,
+                                   const void* Q, const void* D, const uint8_t* qmask,
+                                   const int32_t* args, int dim, int Tq, int Td, int B,
+                                   void* dQ, void* dD, fms_stream_t stream);
 
 /* backward_layouts.jl:96-128 (inbatch_pullback_ka). Delta (Bd,Bq), inv_n (Bq,). */
 int fms_inbatch_bwd(int dtype, int strategy, const void* Delta, const void* inv_n,
