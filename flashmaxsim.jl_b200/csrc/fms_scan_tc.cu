@@ -627,9 +627,16 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           }
         }
       }
-      // finish the rows: exact first-valid rule, tape, per-row contribution
+      // finish the rows: exact first-valid rule, tape, per-row contribution.
+      // One query of <= 32 rows with R = 4: the rows are the lanes of the copy-0
+      // warp, which sums them itself (butterfly; no shared-memory round trip and
+      // no second epilogue barrier).  Otherwise rows go through red_s and one
+      // thread per query sums them in t order.
+      const bool one_warp = (R == 4) && (m.nq == 1);
+      float rowv[MAXMT];
 #pragma unroll
       for (int mt = 0; mt < MAXMT; ++mt) {
+        rowv[mt] = 0.f;
         const int r = mt * M + lr;
         if (mt < nmt && lr >= 0 && h == 0 && r < rows) {
           const int qi = r / m.Tq, t = r - qi * m.Tq;
@@ -646,37 +653,56 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             if (first >= 0 && s0[mt] != s0[mt]) v = s0[mt];
             ok = tv && first >= 0;
           }
-          red_s[ub][r] = ok ? v : 0.f;
+          rowv[mt] = ok ? v : 0.f;
+          if (!one_warp) red_s[ub][r] = rowv[mt];
           if (ARGS) p.args[m.arg0 + qi * m.arg_stride + t] = ok ? a : 0;
         }
       }
-      __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(&epi_bar);
-      if (!ptx::warp_wait(&epi_bar, ephase, &abort_s)) goto done;
-      ephase ^= 1;
-      if (et < m.nq) {
-        const int qi = et;
-        const float* rs = red_s[ub] + qi * m.Tq;
-        float score = 0.f;
-        int nvalid = 0;
-        // Sigma_t in t order (forward_pair.jl:92-95)
-        if ((m.Tq & 3) == 0) {
-          for (int t = 0; t < m.Tq; t += 4) {
-            const float4 v4 = *reinterpret_cast<const float4*>(rs + t);
-            score += v4.x;
-            score += v4.y;
-            score += v4.z;
-            score += v4.w;
+      if (one_warp) {
+        if (h == 0) {
+          float sum = rowv[0];
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+          if (lane == 0) {
+            if (p.normalize) {
+              const uint32_t vm = m.Tq >= 32 ? 0xffffffffu : ((1u << m.Tq) - 1u);
+              const int nvalid = __popc(m.qw[0] & vm);
+              sum = sum * (1.0f / (float)(nvalid > 1 ? nvalid : 1));
+            }
+            scores[m.out0] = sum;
           }
-        } else {
-          for (int t = 0; t < m.Tq; ++t) score += rs[t];
         }
-        for (int t = 0; t < m.Tq; ++t) {
-          const int r = qi * m.Tq + t;
-          nvalid += (m.qw[r >> 5] >> (r & 31)) & 1u;
+      } else {
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&epi_bar);
+        if (!ptx::warp_wait(&epi_bar, ephase, &abort_s)) goto done;
+        ephase ^= 1;
+        if (et < m.nq) {
+          const int qi = et;
+          const float* rs = red_s[ub] + qi * m.Tq;
+          float score = 0.f;
+          // Sigma_t in t order (forward_pair.jl:92-95)
+          if ((m.Tq & 3) == 0) {
+            for (int t = 0; t < m.Tq; t += 4) {
+              const float4 v4 = *reinterpret_cast<const float4*>(rs + t);
+              score += v4.x;
+              score += v4.y;
+              score += v4.z;
+              score += v4.w;
+            }
+          } else {
+            for (int t = 0; t < m.Tq; ++t) score += rs[t];
+          }
+          if (p.normalize) {
+            int nvalid = 0;
+            for (int t = 0; t < m.Tq; ++t) {
+              const int r = qi * m.Tq + t;
+              nvalid += (m.qw[r >> 5] >> (r & 31)) & 1u;
+            }
+            score = score * (1.0f / (float)(nvalid > 1 ? nvalid : 1));
+          }
+          scores[m.out0 + qi * m.out_stride] = score;
         }
-        if (p.normalize) score = score * (1.0f / (float)(nvalid > 1 ? nvalid : 1));
-        scores[m.out0 + qi * m.out_stride] = score;
       }
       if (ARGS)
         for (int t = m.Tq + et; t < m.arg_rows; t += 128) p.args[m.arg0 + t] = 0;
