@@ -51,6 +51,8 @@ def parse():
     # line itself always uses the defaults
     ap.add_argument("--ndoc", type=int, default=NDOC)
     ap.add_argument("--ncand", type=int, default=C)
+    # the other BASELINE.json configs (measured one at a time; the default line is c2)
+    ap.add_argument("--workload", default="c2", choices=["c1", "c2", "c3", "c4", "c5"])
     return ap.parse_args()
 
 
@@ -264,6 +266,13 @@ def main():
     args = parse()
     NDOC, C = args.ndoc, args.ncand
     world, rank, local = dist_setup(args)
+    if args.workload != "c2":
+        import bench_configs
+        bench_configs.run(args, world, rank, local)
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        return
     if args.impl == "reference":
         run_reference(args, world, rank)
         if world > 1:

@@ -1,0 +1,627 @@
+"""bench.py --workload c1|c3|c4|c5: the other BASELINE.json configurations.
+
+The default bench line is c2 (bench.py).  These runs measure the remaining
+configs one at a time with the same JSON keys (metric, value, e2e, roofline,
+clocks, cpu_baseline); each docstring below states its workload and units.
+
+  c1  paired f32 fwd+bwd (AtomicUnified, Delta = ones), Q (32,32,128),
+      D (32,180,128): doc-tokens/s; inputs fit in L2, so L2 is flushed between
+      timed steps (outside the per-step events).
+  c3  in-batch bf16 training step: S = maxsim(Q, D, InBatch()) with Bq = Bd =
+      256, Tq 32, Td 180 (valid U[32,180]), dim 768, then the InvGrid pullback
+      of a N(0,1) dS: steps/s; inputs (83 MB) fit in L2 -> flushed between steps.
+  c4  packed varlen scan f16: 16 queries x 24 tokens x 128 against 50,000 docs
+      of U[700,1030] tokens (11 GB, larger than L2): doc-tokens/s.
+  c5  INT8 exhaustive search: 32 fp16 queries x 32 x 128, quantized on the
+      device every step, against 1,000,000 docs x 128 tokens int8 + f32 scales
+      (16.9 GB), top-100 per query: doc-tokens/s.
+
+N > 1 (torchrun) for c4 / c5: the documents are split into contiguous ranges,
+one per rank (strong scaling: the total is the config's); c4 all-gathers the
+score blocks and c5 all-gathers and merges the per-rank top-100 lists.
+"""
+from __future__ import annotations
+
+import json
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import bench as B  # noqa: E402  (ClockSampler, measured peaks)
+
+UNIT_TOK = "doc-tokens/s"
+L2_FLUSH_BYTES = 512 << 20  # > 126 MB of L2
+
+
+def l2n(x):
+    return x / x.norm(dim=-1, keepdim=True)
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm": float(d["hbm_gbs"]), "bf16": float(d["bf16_tflops"]),
+                "bf16_sus": float(d["bf16_tflops_sustained"]), "src": "measured"}
+    return {"hbm": 6650.0, "bf16": 1590.0, "bf16_sus": 1400.0, "src": "fallback"}
+
+
+class Timer:
+    """Per-step CUDA events on the current stream, with an optional L2 flush
+    (a write larger than L2) between steps, outside the timed events."""
+
+    def __init__(self, dev, flush):
+        self.dev = dev
+        self.flush_buf = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev) if flush else None
+
+    def run(self, fn, steps, parts=None):
+        """Returns total ms over `steps`, and per-part totals when fn records
+        marks through the `mark` callback it receives."""
+        tot = 0.0
+        part_ms = {}
+        for _ in range(steps):
+            if self.flush_buf is not None:
+                self.flush_buf.fill_(1)
+            marks = []
+
+            def mark(name):
+                e = torch.cuda.Event(enable_timing=True)
+                e.record()
+                marks.append((name, e))
+
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn(mark)
+            e1.record()
+            torch.cuda.synchronize()
+            tot += e0.elapsed_time(e1)
+            prev = e0
+            for name, e in marks:
+                part_ms[name] = part_ms.get(name, 0.0) + prev.elapsed_time(e)
+                prev = e
+        return tot, part_ms
+
+
+def max_over_ranks(x, world, dev):
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.item()
+
+
+def base_line(args, world, metric, value, unit, ms_step, dtype, config, hib=True, scaling="strong"):
+    return {"metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": hib,
+            "scaling": scaling, "vs_baseline": None, "dtype": dtype,
+            "data": "synthetic (seeded randn, L2-normalised tokens; no dataset in the reference)",
+            "config": config}
+
+
+def oracle():
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle as O
+    return O
+
+
+def time_cpu(fn, min_seconds=10.0):
+    fn()  # warm
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        fn()
+        reps += 1
+        if time.perf_counter() - t0 >= min_seconds:
+            break
+    return (time.perf_counter() - t0) / reps, reps
+
+
+# --------------------------------------------------------------------------- c1
+
+def c1_inputs(dev):
+    g = torch.Generator(device="cpu").manual_seed(11)
+    Q = l2n(torch.randn(32, 32, 128, generator=g))
+    D = l2n(torch.randn(32, 180, 128, generator=g))
+    return Q.to(dev), D.to(dev)
+
+
+def run_c1(args, world, rank, local, dev, fms):
+    Q, D = c1_inputs(dev)
+    ntok = 32 * 180
+    ones = torch.ones(32, dtype=torch.float32, device=dev)
+    cfg = {"workload": "c1 paired f32 fwd+bwd (AtomicUnified, Delta=ones): Q 32x32x128, "
+                       "D 32x180x128, all masks true",
+           "doc_tokens_per_step": ntok, "l2": "inputs fit in L2: 512 MB flush between steps",
+           "parallelism": f"replicas only ({world} GPU(s))"}
+    if args.impl == "reference":
+        O = oracle()
+        Qn, Dn = Q.cpu().numpy(), D.cpu().numpy()
+        thr = O.default_threads()
+
+        def cpu_step():
+            S, a = O.paired(Qn, Dn, nthreads=thr)
+            O.paired_pullback(np.ones(32, np.float32), None, Qn, Dn, None, a, 0)
+        dt, reps = time_cpu(cpu_step, min_seconds=max(2.0, 0.0))
+        v = ntok / dt
+        line = base_line(args, world, "doc-tokens scored/sec (fwd+bwd)", v, UNIT_TOK, dt * 1e3,
+                         "f32", cfg)
+        line.update(impl="reference",
+                    cpu_baseline={"value": v, "unit": UNIT_TOK, "cores": thr, "kind": "port",
+                                  "sample": f"the whole c1 step, {reps} repetitions"},
+                    e2e={"value": v, "unit": UNIT_TOK, "h2d_bytes_per_step": 0,
+                         "d2h_bytes_per_step": 0})
+        print(json.dumps(line))
+        return
+
+    def step(mark):
+        S, a = fms.paired_forward(Q, D, want_args=True)
+        mark("fwd")
+        fms.paired_pullback(ones, Q, D, None, a, None, fms.AtomicUnified())
+        mark("bwd")
+
+    tm = Timer(dev, flush=True)
+    tm.run(step, max(3, args.warmup))
+    clocks = B.ClockSampler(local)
+    clocks.start()
+    ms, parts = tm.run(step, args.steps)
+    clk = clocks.stop()
+    ms = max_over_ranks(ms, world, dev)
+    ms_step = ms / args.steps
+    value = world * ntok * args.steps / (ms / 1e3)
+    # e2e through the public API with host buffers (autograd, Delta = ones)
+    Qh, Dh = Q.cpu().pin_memory(), D.cpu().pin_memory()
+    Sh = torch.empty(32, dtype=torch.float32).pin_memory()
+
+    def e2e_step(mark):
+        q = Qh.to(dev, non_blocking=True).requires_grad_()
+        d = Dh.to(dev, non_blocking=True).requires_grad_()
+        S = fms.maxsim(q, d)
+        S.backward(ones)
+        Sh.copy_(S.detach(), non_blocking=True)
+
+    tm.run(e2e_step, 2)
+    te, _ = tm.run(e2e_step, args.steps)
+    te = max_over_ranks(te, world, dev)
+    alg_bytes = (Q.numel() + D.numel()) * 4 * 2 + 32 * 32 * 4  # fwd reads + bwd reads/writes
+    line = base_line(args, world, "doc-tokens scored/sec (fwd+bwd)", value, UNIT_TOK, ms_step,
+                     "f32", cfg, scaling="weak")
+    line["e2e"] = {"value": world * ntok * args.steps / (te / 1e3), "unit": UNIT_TOK,
+                   "h2d_bytes_per_step": (Q.numel() + D.numel()) * 4, "d2h_bytes_per_step": 128}
+    line["gpu_launches"] = args.steps * 4
+    line["roofline"] = {"bound": "latency", "achieved": alg_bytes / (ms_step / 1e3) / 1e9,
+                        "peak": peaks()["hbm"], "unit": "GB/s",
+                        "frac": alg_bytes / (ms_step / 1e3) / 1e9 / peaks()["hbm"],
+                        "traffic": None, "kernel": "paired SIMT scan + AtomicUnified backward",
+                        "note": "5,760 doc-tokens per step: a single latency-bound launch pair",
+                        "fwd_ms": parts.get("fwd", 0) / args.steps,
+                        "bwd_ms": parts.get("bwd", 0) / args.steps}
+    line["clocks"] = clk
+    if rank == 0 and not args.no_cpu_baseline:
+        O = oracle()
+        Qn, Dn = Q.cpu().numpy(), D.cpu().numpy()
+
+        def cpu_step():
+            S, a = O.paired(Qn, Dn, nthreads=1)
+            O.paired_pullback(np.ones(32, np.float32), None, Qn, Dn, None, a, 0)
+        dt, reps = time_cpu(cpu_step, min_seconds=2.0)
+        line["cpu_baseline"] = {"value": ntok / dt, "unit": UNIT_TOK, "cores": 1, "kind": "port",
+                                "sample": f"the whole c1 step, serial as the reference runs it, "
+                                          f"{reps} repetitions"}
+    if rank == 0:
+        print(json.dumps(line))
+
+
+# --------------------------------------------------------------------------- c3
+
+BQ3, BD3, TQ3, TD3, DIM3 = 256, 256, 32, 180, 768
+
+
+def c3_inputs(dev):
+    g = torch.Generator(device=dev)
+    g.manual_seed(33)
+    Q = l2n(torch.randn(BQ3, TQ3, DIM3, generator=g, device=dev)).to(torch.bfloat16)
+    D = l2n(torch.randn(BD3, TD3, DIM3, generator=g, device=dev)).to(torch.bfloat16)
+    lens = torch.randint(32, TD3 + 1, (BD3,), generator=g, device=dev)
+    dmask = torch.arange(TD3, device=dev)[None, :] < lens[:, None]
+    dS = torch.randn(BQ3, BD3, generator=g, device=dev)
+    return Q, D, dmask, lens, dS
+
+
+def c3_config(world, lens_sum):
+    return {"workload": "c3 in-batch bf16 training step (fwd + InvGrid bwd): Bq=Bd=256, Tq 32, "
+                        "Td 180 (valid U[32,180]), dim 768, dS ~ N(0,1)",
+            "valid_doc_tokens": lens_sum,
+            "l2": "inputs (83 MB) fit in L2: 512 MB flush between steps (outside the events)",
+            "parallelism": f"replicas ({world} GPU(s))"}
+
+
+def run_c3(args, world, rank, local, dev, fms):
+    Q, D, dmask, lens, dS = c3_inputs(dev)
+    Lsum = int(lens.sum().item())
+    cfg = c3_config(world, Lsum)
+    fwd_flop = 2.0 * BQ3 * TQ3 * DIM3 * Lsum
+    if args.impl == "reference":
+        O = oracle()
+        thr = O.default_threads()
+        nsq = 8
+        Qn, Dn = Q[:nsq].float().cpu().numpy(), D.float().cpu().numpy()
+        dm, dSn = dmask.cpu().numpy(), dS[:nsq].cpu().numpy()
+
+        def cpu_step():
+            S, a = O.inbatch(Qn, Dn, None, dm, nthreads=thr)
+            O.inbatch_pullback(dSn, None, Qn, Dn, None, a, 1, dtype_code=2)
+        dt, reps = time_cpu(cpu_step, min_seconds=5.0)
+        full = dt * BQ3 / nsq
+        v = 1.0 / full
+        line = base_line(args, world, "in-batch fwd+bwd steps/sec", v, "steps/s", full * 1e3,
+                         "f32", cfg)
+        line.update(impl="reference",
+                    cpu_baseline={"value": v, "unit": "steps/s", "cores": thr, "kind": "port",
+                                  "sample": f"{nsq} of 256 queries x all 256 docs (fwd + InvGrid "
+                                            f"bwd), {reps} repetitions, scaled x{BQ3 // nsq}"},
+                    e2e={"value": v, "unit": "steps/s", "h2d_bytes_per_step": 0,
+                         "d2h_bytes_per_step": 0})
+        print(json.dumps(line))
+        return
+
+    inv = None  # normalize=False: inv_n is not applied (rrule.jl:106-112)
+
+    def step(mark):
+        S, a = fms.inbatch_forward(Q, D, None, dmask, want_args=True)
+        mark("fwd")
+        fms.inbatch_pullback(dS, Q, D, None, a, inv, fms.InvGrid())
+        mark("bwd")
+
+    def fwd_only(mark):
+        fms.inbatch_forward(Q, D, None, dmask, want_args=False)
+
+    tm = Timer(dev, flush=True)
+    tm.run(step, max(3, args.warmup))
+    clocks = B.ClockSampler(local)
+    clocks.start()
+    ms, parts = tm.run(step, args.steps)
+    clk = clocks.stop()
+    tm.run(fwd_only, 3)
+    ms_f, _ = tm.run(fwd_only, args.steps)
+    ms = max_over_ranks(ms, world, dev)
+    ms_step = ms / args.steps
+    value = world * args.steps / (ms / 1e3)
+    # e2e: public API with host buffers; inputs in, S out
+    Qh, Dh = Q.cpu().pin_memory(), D.cpu().pin_memory()
+    mh, gh = dmask.cpu().pin_memory(), dS.cpu().pin_memory()
+    Sh = torch.empty((BQ3, BD3), dtype=torch.float32).pin_memory()
+
+    def e2e_step(mark):
+        q = Qh.to(dev, non_blocking=True).requires_grad_()
+        d = Dh.to(dev, non_blocking=True).requires_grad_()
+        m = mh.to(dev, non_blocking=True)
+        g = gh.to(dev, non_blocking=True)
+        S = fms.maxsim(q, d, None, m, fms.InBatch(), backward=fms.InvGrid())
+        S.backward(g)
+        Sh.copy_(S.detach(), non_blocking=True)
+
+    tm.run(e2e_step, 2)
+    te, _ = tm.run(e2e_step, args.steps)
+    te = max_over_ranks(te, world, dev)
+    pk = peaks()
+    fwd_ms = ms_f / args.steps
+    achieved = fwd_flop / (fwd_ms / 1e3) / 1e12
+    line = base_line(args, world, "in-batch fwd+bwd steps/sec", value, "steps/s", ms_step, "bf16",
+                     cfg, scaling="weak")
+    line["e2e"] = {"value": world * args.steps / (te / 1e3), "unit": "steps/s",
+                   "h2d_bytes_per_step": Q.numel() * 2 + D.numel() * 2 + dmask.numel() + dS.numel() * 4,
+                   "d2h_bytes_per_step": BQ3 * BD3 * 4}
+    line["gpu_launches"] = None
+    line["roofline"] = {"bound": "tensor", "achieved": achieved, "peak": pk["bf16"],
+                        "unit": "TFLOP/s", "frac": achieved / pk["bf16"], "traffic": None,
+                        "peak_source": f"{pk['src']} bf16_tflops (burst; the kernel is timed alone)",
+                        "kernel": "in-batch forward scan (scores-only launch)",
+                        "algorithmic_flop_per_launch": fwd_flop,
+                        "fwd_ms_with_tape": parts.get("fwd", 0) / args.steps,
+                        "fwd_ms_scores_only": fwd_ms,
+                        "bwd_ms": parts.get("bwd", 0) / args.steps}
+    line["clocks"] = clk
+    if rank == 0 and not args.no_cpu_baseline:
+        O = oracle()
+        nsq = 8
+        Qn, Dn = Q[:nsq].float().cpu().numpy(), D.float().cpu().numpy()
+        dm, dSn = dmask.cpu().numpy(), dS[:nsq].cpu().numpy()
+        thr = O.default_threads()
+
+        def cpu_step():
+            S, a = O.inbatch(Qn, Dn, None, dm, nthreads=thr)
+            O.inbatch_pullback(dSn, None, Qn, Dn, None, a, 1, dtype_code=2)
+        dt, reps = time_cpu(cpu_step, min_seconds=5.0)
+        line["cpu_baseline"] = {"value": nsq / BQ3 / dt, "unit": "steps/s", "cores": thr,
+                                "kind": "port",
+                                "sample": f"{nsq} of 256 queries x all 256 docs (fwd + InvGrid "
+                                          f"bwd, f32 on bf16-rounded inputs), {reps} repetitions, "
+                                          f"scaled to 256 queries"}
+    if rank == 0:
+        print(json.dumps(line))
+
+
+# --------------------------------------------------------------------------- c4
+
+NQ4, TQ4, DIM4, NDOC4 = 16, 24, 128, 50_000
+
+
+def c4_inputs(dev, fms, world, rank):
+    g = torch.Generator(device=dev)
+    g.manual_seed(44)
+    lens = torch.randint(700, 1031, (NDOC4,), generator=g, device=dev)
+    gq = torch.Generator(device=dev)
+    gq.manual_seed(45)
+    Qs = l2n(torch.randn(NQ4, TQ4, DIM4, generator=gq, device=dev)).half()
+    lo = NDOC4 * rank // world
+    hi = NDOC4 * (rank + 1) // world
+    my = lens[lo:hi]
+    ntok = int(my.sum().item())
+    tokens = torch.empty((ntok, DIM4), dtype=torch.float16, device=dev)
+    g2 = torch.Generator(device=dev)
+    g2.manual_seed(46 + rank)
+    step = 1 << 22
+    for r0 in range(0, ntok, step):
+        r1 = min(ntok, r0 + step)
+        tokens[r0:r1] = l2n(torch.randn((r1 - r0, DIM4), generator=g2, device=dev)).half()
+    cu = torch.zeros(hi - lo + 1, dtype=torch.int64, device=dev)
+    cu[1:] = torch.cumsum(my, 0)
+    cu = (cu + 1).to(torch.int32)
+    P = fms.make_packed(tokens, cu)
+    counts = [NDOC4 * (r + 1) // world - NDOC4 * r // world for r in range(world)]
+    return Qs, P, ntok, counts
+
+
+def run_c4(args, world, rank, local, dev, fms):
+    Qs, P, ntok, counts = c4_inputs(dev, fms, world, rank)
+    cfg = {"workload": "c4 packed varlen scan f16: 16 q x 24 tok x 128 dim vs PackedSeq of 50000 "
+                       "docs, len U[700,1030], 1-based cu",
+           "l2": "inputs larger than L2 (11 GB of tokens per step)",
+           "parallelism": f"contiguous doc ranges over {world} GPU(s)" +
+                          (", NCCL all-gather of score blocks" if world > 1 else "")}
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        O = oracle()
+        thr = O.default_threads()
+        nb = 200
+        cu = P.cu[:nb + 1].cpu().numpy()
+        toks = P.tokens[:int(cu[-1]) - 1].float().cpu().numpy()
+        Qn = Qs.float().cpu().numpy()
+        stok = NQ4 * (int(cu[-1]) - 1)
+        dt, reps = time_cpu(lambda: O.packed(Qn, toks, cu, nthreads=thr), min_seconds=5.0)
+        v = stok / dt
+        line = base_line(args, world, "doc-tokens scored/sec", v, UNIT_TOK, dt * 1e3, "f32", cfg)
+        line.update(impl="reference",
+                    cpu_baseline={"value": v, "unit": UNIT_TOK, "cores": thr, "kind": "port",
+                                  "sample": f"all 16 queries x the first {nb} docs per step"},
+                    e2e={"value": v, "unit": UNIT_TOK, "h2d_bytes_per_step": 0,
+                         "d2h_bytes_per_step": 0})
+        print(json.dumps(line))
+        return
+    from flashmaxsim_b200 import dist as fdist
+
+    def scan():
+        return fms.packed_forward(Qs, P, want_args=False)[0]
+
+    def step(mark):
+        S = scan()
+        if world > 1:
+            fdist.gather_packed_scores(S, counts)
+
+    tm = Timer(dev, flush=False)
+    tm.run(step, max(3, args.warmup))
+    clocks = B.ClockSampler(local)
+    clocks.start()
+    ms, _ = tm.run(step, args.steps)
+    clk = clocks.stop()
+    kms, _ = tm.run(lambda m: scan(), args.steps)
+    ms = max_over_ranks(ms, world, dev)
+    tok_all = torch.tensor([ntok], dtype=torch.float64, device=dev)
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(tok_all)
+    tot_tok = tok_all.item()
+    ms_step = ms / args.steps
+    value = NQ4 * tot_tok * args.steps / (ms / 1e3)
+    Qh = Qs.cpu().pin_memory()
+    Sh = torch.empty((NQ4, NDOC4), dtype=torch.float32).pin_memory()
+
+    def e2e_step(mark):
+        q = Qh.to(dev, non_blocking=True)
+        S = fms.maxsim(q, P)
+        if world > 1:
+            S = fdist.gather_packed_scores(S, counts)
+        Sh.copy_(S, non_blocking=True)
+
+    tm.run(e2e_step, 2)
+    te, _ = tm.run(e2e_step, args.steps)
+    te = max_over_ranks(te, world, dev)
+    pk = peaks()
+    kms_step = kms / args.steps
+    flop = 2.0 * NQ4 * TQ4 * DIM4 * ntok
+    byts = ntok * DIM4 * 2 + P.cu.numel() * 4 + Qs.numel() * 2 + NQ4 * P.cu.numel() * 4
+    t_hbm = byts / (pk["hbm"] * 1e9)
+    t_tc = flop / (pk["bf16"] * 1e12)
+    tc_bound = t_tc >= t_hbm
+    achieved = (flop / 1e12 if tc_bound else byts / 1e9) / (kms_step / 1e3)
+    peak = pk["bf16"] if tc_bound else pk["hbm"]
+    line = base_line(args, world, "doc-tokens scored/sec", value, UNIT_TOK, ms_step, "f16", cfg)
+    line["config"]["doc_tokens_per_step"] = NQ4 * tot_tok
+    line["e2e"] = {"value": NQ4 * tot_tok * args.steps / (te / 1e3), "unit": UNIT_TOK,
+                   "h2d_bytes_per_step": Qh.numel() * 2, "d2h_bytes_per_step": Sh.numel() * 4}
+    line["gpu_launches"] = args.steps
+    line["roofline"] = {"bound": "tensor" if tc_bound else "hbm", "achieved": achieved,
+                        "peak": peak, "unit": "TFLOP/s" if tc_bound else "GB/s",
+                        "frac": achieved / peak, "traffic": None,
+                        "peak_source": f"{pk['src']} " + ("bf16_tflops" if tc_bound else "hbm_gbs"),
+                        "kernel": "packed scan (16 queries stacked per document)",
+                        "algorithmic_flop_per_launch": flop, "algorithmic_bytes_per_launch": byts,
+                        "hbm_frac": byts / (kms_step / 1e3) / 1e9 / pk["hbm"],
+                        "tensor_frac": flop / (kms_step / 1e3) / 1e12 / pk["bf16"],
+                        "kernel_ms": kms_step}
+    line["clocks"] = clk
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        O = oracle()
+        thr = O.default_threads()
+        nb = 200
+        cu = P.cu[:nb + 1].cpu().numpy()
+        toks = P.tokens[:int(cu[-1]) - 1].float().cpu().numpy()
+        Qn = Qs.float().cpu().numpy()
+        stok = NQ4 * (int(cu[-1]) - 1)
+        dt, reps = time_cpu(lambda: O.packed(Qn, toks, cu, nthreads=thr), min_seconds=10.0)
+        line["cpu_baseline"] = {"value": stok / dt, "unit": UNIT_TOK, "cores": thr, "kind": "port",
+                                "sample": f"all 16 queries x the first {nb} docs "
+                                          f"({stok} doc-tokens per pass, {reps} passes)"}
+    if rank == 0:
+        print(json.dumps(line))
+
+
+# --------------------------------------------------------------------------- c5
+
+NQ5, TQ5, DIM5, NDOC5, TD5, K5 = 32, 32, 128, 1_000_000, 128, 100
+
+
+def c5_inputs(dev, fms, world, rank, ndoc):
+    lo = ndoc * rank // world
+    hi = ndoc * (rank + 1) // world
+    n = hi - lo
+    codes = torch.empty((n, TD5, DIM5), dtype=torch.int8, device=dev)
+    scales = torch.empty((n, TD5), dtype=torch.float32, device=dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(55 + rank)
+    chunk = 16384
+    for j0 in range(0, n, chunk):
+        j1 = min(n, j0 + chunk)
+        x = l2n(torch.randn((j1 - j0, TD5, DIM5), generator=g, device=dev))
+        qi = fms.quantize_int8_symmetric(x)
+        codes[j0:j1] = qi.codes
+        scales[j0:j1] = qi.scales
+        del x, qi
+    gq = torch.Generator(device=dev)
+    gq.manual_seed(56)
+    Q = l2n(torch.randn(NQ5, TQ5, DIM5, generator=gq, device=dev)).half()
+    return Q, fms.Int8Index(codes, scales), lo + 1
+
+
+def run_c5(args, world, rank, local, dev, fms):
+    ndoc = args.ndoc if args.ndoc != B.NDOC else NDOC5
+    Q, index, shard_lo = c5_inputs(dev, fms, world, rank, ndoc)
+    n = index.codes.shape[0]
+    cfg = {"workload": f"c5 INT8 exhaustive search: 32 fp16 q x 32 tok x 128 (quantized on the "
+                       f"device each step) vs {ndoc} docs x 128 tok int8 + f32 scales, top-100",
+           "l2": "inputs larger than L2 (16.9 GB index per step)",
+           "parallelism": f"index sharded by doc id over {world} GPU(s)" +
+                          (", NCCL all-gather + device merge of top-100" if world > 1 else "")}
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        O = oracle()
+        thr = O.default_threads()
+        nb = 4000
+        qq = fms.quantize_int8_symmetric(Q)
+        Qc, Qsc = qq.codes.cpu().numpy(), qq.scales.float().cpu().numpy()
+        Gc, Gs = index.codes[:nb].cpu().numpy(), index.scales[:nb].cpu().numpy()
+        stok = NQ5 * nb * TD5
+        dt, reps = time_cpu(lambda: O.int8_exhaustive(Qc, Qsc, Gc, Gs, nthreads=thr),
+                            min_seconds=5.0)
+        v = stok / dt
+        line = base_line(args, world, "doc-tokens scored/sec", v, UNIT_TOK, dt * 1e3, "int8", cfg)
+        line.update(impl="reference",
+                    cpu_baseline={"value": v, "unit": UNIT_TOK, "cores": thr, "kind": "port",
+                                  "sample": f"32 queries x the first {nb} docs per step (scores; "
+                                            f"top-k selection not timed)"},
+                    e2e={"value": v, "unit": UNIT_TOK, "h2d_bytes_per_step": 0,
+                         "d2h_bytes_per_step": 0})
+        print(json.dumps(line))
+        return
+    from flashmaxsim_b200 import dist as fdist
+
+    def search(q):
+        vals, ids = fms.int8_exhaustive_forward(q, index, topk=K5, id_offset=shard_lo - 1)
+        if world > 1:
+            vals, ids = fdist.merge_topk(vals, ids, K5)
+        return vals, ids
+
+    def step(mark):
+        search(Q)
+
+    tm = Timer(dev, flush=False)
+    tm.run(step, max(3, args.warmup))
+    clocks = B.ClockSampler(local)
+    clocks.start()
+    ms, _ = tm.run(step, args.steps)
+    clk = clocks.stop()
+    qq = fms.quantize_int8_symmetric(Q)
+    kms, _ = tm.run(lambda m: fms.int8_exhaustive_forward(None, index, topk=K5, quantized=qq),
+                    args.steps)
+    ms = max_over_ranks(ms, world, dev)
+    ms_step = ms / args.steps
+    tot_tok = NQ5 * ndoc * TD5
+    value = tot_tok * args.steps / (ms / 1e3)
+    Qh = Q.cpu().pin_memory()
+    vh = torch.empty((NQ5, K5), dtype=torch.float32).pin_memory()
+    ih = torch.empty((NQ5, K5), dtype=torch.int32).pin_memory()
+
+    def e2e_step(mark):
+        q = Qh.to(dev, non_blocking=True)
+        vals, ids = fms.maxsim(q, index, topk=K5) if world == 1 else search(q)
+        vh.copy_(vals, non_blocking=True)
+        ih.copy_(ids, non_blocking=True)
+
+    tm.run(e2e_step, 2)
+    te, _ = tm.run(e2e_step, args.steps)
+    te = max_over_ranks(te, world, dev)
+    pk = peaks()
+    kms_step = kms / args.steps
+    ops = 2.0 * NQ5 * TQ5 * DIM5 * n * TD5
+    byts = n * TD5 * (DIM5 + 4)
+    int8_peak = 2.0 * pk["bf16"]
+    achieved = ops / (kms_step / 1e3) / 1e12
+    line = base_line(args, world, "doc-tokens scored/sec", value, UNIT_TOK, ms_step, "int8", cfg)
+    line["config"]["doc_tokens_per_step"] = tot_tok
+    line["e2e"] = {"value": tot_tok * args.steps / (te / 1e3), "unit": UNIT_TOK,
+                   "h2d_bytes_per_step": Qh.numel() * 2, "d2h_bytes_per_step": NQ5 * K5 * 8}
+    line["gpu_launches"] = None
+    line["roofline"] = {"bound": "tensor", "achieved": achieved, "peak": int8_peak,
+                        "unit": "TOP/s", "frac": achieved / int8_peak, "traffic": None,
+                        "peak_source": f"2 x {pk['src']} bf16_tflops (B200 dense int8 rate is "
+                                       "twice bf16; no measured int8 peak)",
+                        "kernel": "INT8 exhaustive scan + top-100",
+                        "algorithmic_ops_per_launch": ops, "algorithmic_bytes_per_launch": byts,
+                        "hbm_frac": byts / (kms_step / 1e3) / 1e9 / pk["hbm"],
+                        "kernel_ms": kms_step}
+    line["clocks"] = clk
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        O = oracle()
+        thr = O.default_threads()
+        nb = 4000
+        Qc, Qsc = qq.codes.cpu().numpy(), qq.scales.float().cpu().numpy()
+        Gc, Gs = index.codes[:nb].cpu().numpy(), index.scales[:nb].cpu().numpy()
+        stok = NQ5 * nb * TD5
+        dt, reps = time_cpu(lambda: O.int8_exhaustive(Qc, Qsc, Gc, Gs, nthreads=thr),
+                            min_seconds=10.0)
+        line["cpu_baseline"] = {"value": stok / dt, "unit": UNIT_TOK, "cores": thr, "kind": "port",
+                                "sample": f"32 queries x the first {nb} docs ({stok} doc-tokens "
+                                          f"per pass, {reps} passes; scores only, no top-k)"}
+    if rank == 0:
+        print(json.dumps(line))
+
+
+def run(args, world, rank, local):
+    if not torch.cuda.is_available():
+        print(json.dumps({"impl": args.impl, "unavailable": "no CUDA device"}))
+        return
+    dev = torch.device("cuda", local)
+    import flashmaxsim_b200 as fms
+    fn = {"c1": run_c1, "c3": run_c3, "c4": run_c4, "c5": run_c5}[args.workload]
+    if args.impl == "reference" and args.workload in ("c1", "c3") and rank != 0:
+        return
+    fn(args, world, rank, local, dev, fms)
