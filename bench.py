@@ -53,6 +53,7 @@ def parse():
     ap.add_argument("--ncand", type=int, default=C)
     # the other BASELINE.json configs (measured one at a time; the default line is c2)
     ap.add_argument("--workload", default="c2", choices=["c1", "c2", "c3", "c4", "c5"])
+    ap.add_argument("--c5-ndoc", type=int, default=0, help="smaller c5 index (profiling)")
     return ap.parse_args()
 
 

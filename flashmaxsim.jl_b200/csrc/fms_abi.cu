@@ -95,7 +95,11 @@ const char* fms_status_string(int status) {
 
 int fms_version(void) { return 100; }
 
-int fms_device_error(int reset) { return read_device_error(reset); }
+int fms_device_error(int reset) {
+  const int a = read_device_error(reset);
+  const int b = read_i8tc_device_error(reset);
+  return a != 0 ? a : b;
+}
 
 int fms_pair_fwd(int dtype, const void* q, const void* d, const uint8_t* qmask,
                  const uint8_t* dmask, int dim, int Tq, int Td, int normalize, void* score,
@@ -456,7 +460,8 @@ int fms_int8_exhaustive_fwd(int qs_dtype, int ds_dtype, const int8_t* Qc, const 
   p.qs_dtype = qs_dtype; p.ds_dtype = ds_dtype;
   p.dim = dim; p.Tq = Tq; p.Td = Td; p.exhaustive = 1; p.N = N; p.nunits = N * nq;
   p.normalize = normalize; p.scores = Sbuf; p.args = nullptr;
-  cudaError_t e = launch_int8_scan(p, s);
+  cudaError_t e = launch_int8_exhaustive_tc(p, s);
+  if (e == cudaErrorNotSupported) e = launch_int8_scan(p, s);
   if (e != cudaSuccess) return (int)e;
   if (k > 0) {
     e = launch_topk(Sbuf, N, nq, k, id_offset, ws, topk_vals, topk_ids, s);

@@ -25,6 +25,13 @@ struct Int8ScanParams {
 cudaError_t launch_quantize(int dtype, const void* x, int dim, int64_t ntok, int8_t* codes,
                             void* scales, cudaStream_t s);
 cudaError_t launch_int8_scan(const Int8ScanParams& p, cudaStream_t s);
+// tcgen05 kind::i8 engine for the exhaustive layout (fms_int8_tc.cu).  Returns
+// cudaErrorNotSupported for shapes it does not take (dim not a multiple of 128
+// or above 256, Tq > 32, Td > 256, unaligned codes, no tape); the caller then
+// runs the SIMT scan, which is also a GPU kernel.
+bool int8_exhaustive_tc_supported(const Int8ScanParams& p);
+cudaError_t launch_int8_exhaustive_tc(const Int8ScanParams& p, cudaStream_t s);
+int read_i8tc_device_error(int reset);
 size_t topk_workspace_bytes(int nq, int64_t N, int k);
 cudaError_t launch_topk(const float* S, int64_t N, int nq, int k, int64_t id_offset, void* ws,
                         float* vals, int32_t* ids, cudaStream_t s);

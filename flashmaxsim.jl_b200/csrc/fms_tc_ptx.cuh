@@ -37,28 +37,45 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// Suspend-time hint of the sleeping waits (ns): a waiting thread sleeps until
+// the phase completes or this much time passes, instead of spinning on the
+// barrier and taking issue slots from warps that do the work.  The wake-up adds
+// latency, so only throughput-bound roles use it.
+constexpr uint32_t WAIT_HINT_NS = 0x10000u;
+
+template <bool SLEEP = false>
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
+  if (SLEEP)
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "n"(WAIT_HINT_NS)
+        : "memory");
+  else
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
   return ok != 0;
 }
 
 // Wait for the phase of `bar` with the given parity.  Gives up (returns false)
 // when *abort is raised by another role or after `limit_ns`, raising *abort.
-// The abort flag and the clock are consulted every 256 polls only, so a wait
-// that ends soon costs nothing but the polls.
+// The abort flag and the clock are consulted every 256 polls (every 8 when each
+// poll may sleep), so a wait that ends soon costs nothing but the polls.
+template <bool SLEEP = false>
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
                                           uint64_t limit_ns = 2000000000ull) {
   uint64_t t0 = 0;
   for (uint32_t it = 0;; ++it) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 255u) == 255u) {
+    if (mbar_try_wait<SLEEP>(bar, parity)) return true;
+    if ((it & (SLEEP ? 7u : 255u)) == (SLEEP ? 7u : 255u)) {
       if (*abort) return false;
       const uint64_t now = globaltimer_ns();
       if (t0 == 0) {
@@ -74,9 +91,10 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 // Warp-uniform bounded wait: lane 0 polls, the verdict is broadcast, and the
 // warp re-converges (so every lane sees the same outcome and the memory ordering
 // lane 0 acquired).  Must be called by all 32 lanes.
+template <bool SLEEP = false>
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
   int ok = 0;
-  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort) ? 1 : 0;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait<SLEEP>(bar, parity, abort) ? 1 : 0;
   ok = __shfl_sync(0xffffffffu, ok, 0);
   __syncwarp();
   return ok != 0;
@@ -175,6 +193,17 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
   d |= (uint64_t)(1024 >> 4) << 32;  // stride between 8-row atoms
   d |= (uint64_t)1 << 46;            // descriptor version for sm_100
   d |= (uint64_t)2 << 61;            // SWIZZLE_128B
+  return d;
+}
+
+// Shared-memory matrix descriptor without swizzle: 8-row x 16-byte core
+// matrices, `lbo` bytes between core matrices along K, `sbo` bytes between
+// 8-row groups (0 repeats the same 8 rows across the whole M or N extent).
+__device__ __forceinline__ uint64_t plain_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;            // descriptor version for sm_100; layout 0 = no swizzle
   return d;
 }
 

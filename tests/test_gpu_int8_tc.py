@@ -1,0 +1,104 @@
+"""GPU parity of the tcgen05 kind::i8 exhaustive engine (fms_int8_tc.cu)
+against the oracle's restatement of int8_pair_forward_host (quant.jl:96-125)
+applied to every (query, document) of the index.
+
+Per-token maxima use the reference's formula cell by cell ((qs*ds)*float(acc),
+acc the exact int32 dot product), so with one query token the score is the
+maximum itself and must be bit-identical; with Tq tokens the engine sums the
+maxima in a butterfly rather than in t order, so scores are compared at 1e-5
+relative (the reference's own INT8 tolerance, test_int8.jl:22-44).  Shapes
+cover several queries per pass and several passes, one to four documents per
+MMA, dim 128 and 256, masks, empty documents, normalize, f16 and f32 scales,
+and a NaN scale in and after the first valid column."""
+import numpy as np
+import pytest
+import torch
+
+from conftest import assert_scores, l2cols, seeded
+
+pytestmark = pytest.mark.gpu
+
+
+def _case(fms, rng, nq, Tq, Td, dim, N, qdt=torch.float16, gdt=torch.float32):
+    Q = torch.from_numpy(l2cols(rng.standard_normal((nq, Tq, dim)))).to(qdt).cuda()
+    G = torch.from_numpy(l2cols(rng.standard_normal((N, Td, dim)))).to(gdt).cuda()
+    return Q, fms.quantize_int8_symmetric(G)
+
+
+def _oracle_S(fms, oracle, Q, index, qmask=None, dmask=None, normalize=False):
+    QQ = fms.quantize_int8_symmetric(Q)
+    return oracle.int8_exhaustive(QQ.codes, QQ.scales.float(), index.codes, index.scales.float(),
+                                  None if qmask is None else qmask.cpu(),
+                                  None if dmask is None else dmask.cpu(), normalize=normalize)
+
+
+@pytest.mark.parametrize("nq,Tq,Td,dim,N", [
+    (32, 32, 128, 128, 2001),   # c5 shape: 8 M tiles, 2 documents per stage, odd N
+    (5, 20, 100, 128, 777),     # partial M tile, padded query slots, 128-column doc slots
+    (40, 32, 40, 256, 515),     # dim 256 (two K blocks): several passes, 4 documents per stage
+    (7, 8, 200, 128, 301),      # one 224-column document per stage
+])
+def test_exhaustive_tc_shapes(fms, oracle, nq, Tq, Td, dim, N):
+    rng = seeded(60 + nq)
+    Q, index = _case(fms, rng, nq, Tq, Td, dim, N)
+    S = fms.int8_exhaustive_forward(Q, index)
+    So = _oracle_S(fms, oracle, Q, index)
+    torch.cuda.synchronize()
+    assert_scores(S.cpu(), So, 1e-5)
+
+
+def test_exhaustive_tc_single_token_bit_exact(fms, oracle):
+    """Tq = 1: the score is one dequantised maximum, identical bit for bit."""
+    rng = seeded(61)
+    Q, index = _case(fms, rng, 9, 1, 128, 128, 1500)
+    S = fms.int8_exhaustive_forward(Q, index)
+    So = _oracle_S(fms, oracle, Q, index)
+    assert np.array_equal(S.cpu().numpy(), So)
+
+
+def test_exhaustive_tc_masks_normalize_f16_scales(fms, oracle):
+    rng = seeded(62)
+    nq, Tq, Td, dim, N = 6, 24, 96, 128, 640
+    Q, index = _case(fms, rng, nq, Tq, Td, dim, N, gdt=torch.float16)  # f16 index scales
+    qmask = torch.from_numpy(rng.random((nq, Tq)) > 0.25).cuda()
+    qmask[2] = False                       # query with no valid token -> 0
+    dmask = torch.from_numpy(rng.random((N, Td)) > 0.3).cuda()
+    dmask[7] = False                       # empty document -> 0
+    dmask[8, :90] = False                  # only the tail valid
+    dmask[9, 1:] = False                   # only token 0 valid
+    for normalize in (False, True):
+        S = fms.int8_exhaustive_forward(Q, index, qmask, dmask, normalize=normalize)
+        So = _oracle_S(fms, oracle, Q, index, qmask, dmask, normalize=normalize)
+        assert_scores(S.cpu(), So, 1e-5)
+    assert torch.all(S[:, 7] == 0) and torch.all(S[2] == 0)
+
+
+def test_exhaustive_tc_nan_first_column_sticks(fms, oracle):
+    """arg == 0 || s > mx (quant.jl:110-116): a NaN in the first valid column
+    is kept, a NaN after it never wins."""
+    rng = seeded(63)
+    Q, index = _case(fms, rng, 4, 16, 64, 128, 50)
+    scales = index.scales.clone()
+    scales[3, 0] = float("nan")
+    scales[4, 5] = float("nan")
+    index = fms.Int8Index(index.codes, scales)
+    S = fms.int8_exhaustive_forward(Q, index)
+    So = _oracle_S(fms, oracle, Q, index)
+    assert np.isnan(So[:, 3]).all() and not np.isnan(So[:, 4]).any()
+    assert_scores(S.cpu(), So, 1e-5)
+
+
+def test_exhaustive_tc_topk_matches_oracle_ranking(fms, oracle):
+    rng = seeded(64)
+    nq, k = 32, 100
+    Q, index = _case(fms, rng, nq, 32, 128, 128, 4096)
+    vals, ids, S = fms.int8_exhaustive_forward(Q, index, topk=k, return_scores=True)
+    So = _oracle_S(fms, oracle, Q, index)
+    vo, io = oracle.topk(So, k)
+    # identical lists except where scores tie within the tolerance
+    got = vals.cpu().numpy()
+    assert_scores(got, vo, 1e-5)
+    same = ids.cpu().numpy() == io
+    if not same.all():
+        r, c = np.nonzero(~same)
+        assert np.allclose(So[r, ids.cpu().numpy()[r, c] - 1], vo[r, c], rtol=1e-5, atol=1e-5)
