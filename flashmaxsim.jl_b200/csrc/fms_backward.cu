@@ -285,6 +285,305 @@ csr_scatter_kernel(BwdParams b, const int32_t* __restrict__ row_ptr, const int32
   }
 }
 
+// ------------------------------------------------------------------ vector paths
+//
+// Rows of 16-bit or f32 features move as 16-byte vectors: lane l of a warp
+// owns vectors l, l + 32, ... of a row (NV per lane), so one warp covers a
+// whole row (dim <= 256 * NV * 16 / sizeof(T) bytes) in a single pass over its
+// units or sources, with two rows in flight per warp and registers capped so
+// that two 8-warp blocks share an SM.  The sums run in the same order as the
+// scalar kernels (units ascending, sources ascending), so the results
+// are identical.
+
+template <typename T> struct V16 { static constexpr int E = 16 / (int)sizeof(T); };
+
+__device__ __forceinline__ void unpack(const uint4& v, float (&x)[8], __nv_bfloat16*) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+    x[2 * i] = f.x; x[2 * i + 1] = f.y;
+  }
+}
+__device__ __forceinline__ void unpack(const uint4& v, float (&x)[8], __half*) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+    x[2 * i] = f.x; x[2 * i + 1] = f.y;
+  }
+}
+__device__ __forceinline__ void unpack(const uint4& v, float (&x)[4], float*) {
+  x[0] = __uint_as_float(v.x); x[1] = __uint_as_float(v.y);
+  x[2] = __uint_as_float(v.z); x[3] = __uint_as_float(v.w);
+}
+__device__ __forceinline__ uint4 pack(const float (&x)[8], __nv_bfloat16*) {
+  uint4 v;
+  uint32_t* w = reinterpret_cast<uint32_t*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(x[2 * i], x[2 * i + 1]);
+    w[i] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+  return v;
+}
+__device__ __forceinline__ uint4 pack(const float (&x)[8], __half*) {
+  uint4 v;
+  uint32_t* w = reinterpret_cast<uint32_t*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __half2 h = __floats2half2_rn(x[2 * i], x[2 * i + 1]);
+    w[i] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+  return v;
+}
+__device__ __forceinline__ uint4 pack(const float (&x)[4], float*) {
+  return make_uint4(__float_as_uint(x[0]), __float_as_uint(x[1]), __float_as_uint(x[2]), __float_as_uint(x[3]));
+}
+
+// Source row and delta of one (unit, token) pair, or false when it contributes
+// nothing (masked token, invalid slot, no argmax).  In-batch units of query
+// row r are u = i * Bd + j with i = r / Tq fixed, so the caller passes i and j.
+template <typename T, bool INB>
+__device__ __forceinline__ bool unit_row(const BwdParams& b, int64_t u, int64_t i, int64_t j, int t,
+                                         int64_t& drow, float& dl) {
+  const ScanParams& p = b.g;
+  if constexpr (INB) {
+    if (p.qmask && !p.qmask[i * p.Tq + t]) return false;
+    const int a = p.args[u * p.Tq + t];
+    if (a < 1 || a > p.Td) return false;
+    drow = j * p.Td + a - 1;
+    dl = unit_delta<T>(b, u, (int)i);
+    return true;
+  } else {
+    Unit U = decode_unit(p, u);
+    if (!U.valid || t >= U.Tq || !mask_ok(U.qmask, t)) return false;
+    const int a = p.args[U.arg0 + t];
+    if (a < 1 || a > U.Td) return false;
+    drow = U.d0 + a - 1;
+    dl = unit_delta<T>(b, u, U.qidx);
+    return true;
+  }
+}
+
+// Warp per query-token row: dQ gather (+ dD float32 atomics when ATOMIC).
+constexpr int VEC_UNROLL = 2;  // rows in flight per warp
+
+template <typename T, bool ATOMIC, int NV, bool INB>
+__global__ void __launch_bounds__(256, 2) bwd_gather_vec_kernel(BwdParams b, float* dD_acc) {
+  constexpr int E = V16<T>::E;
+  const ScanParams& p = b.g;
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const uint4* Q = static_cast<const uint4*>(p.Q);
+  const uint4* D = static_cast<const uint4*>(p.D);
+  uint4* dQ = static_cast<uint4*>(b.dQ);
+  const int nvec = p.dim / E;  // 16-byte vectors per row
+  for (int64_t r = warp; r < b.nq_rows; r += nwarps) {
+    int64_t u0, cnt;
+    int t;
+    units_of_row(p, r, u0, cnt, t);
+    const int64_t qi = INB ? r / p.Tq : 0;
+    float acc[NV][E];
+    float qv[NV][E];
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int v = lane + 32 * k;
+#pragma unroll
+      for (int e = 0; e < E; ++e) { acc[k][e] = 0.f; qv[k][e] = 0.f; }
+      if (ATOMIC && v < nvec) unpack(Q[r * nvec + v], qv[k], (T*)nullptr);
+    }
+    for (int64_t i0 = 0; i0 < cnt; i0 += VEC_UNROLL) {
+      int64_t drow[VEC_UNROLL];
+      float dl[VEC_UNROLL];
+      bool ok[VEC_UNROLL];
+#pragma unroll
+      for (int q = 0; q < VEC_UNROLL; ++q) {
+        ok[q] = i0 + q < cnt && unit_row<T, INB>(b, u0 + i0 + q, qi, i0 + q, t, drow[q], dl[q]);
+      }
+      uint4 dv[VEC_UNROLL][NV];
+#pragma unroll
+      for (int q = 0; q < VEC_UNROLL; ++q)
+#pragma unroll
+        for (int k = 0; k < NV; ++k) {
+          const int v = lane + 32 * k;
+          if (ok[q] && v < nvec) dv[q][k] = D[drow[q] * nvec + v];
+        }
+#pragma unroll
+      for (int q = 0; q < VEC_UNROLL; ++q) {
+        if (!ok[q]) continue;
+#pragma unroll
+        for (int k = 0; k < NV; ++k) {
+          const int v = lane + 32 * k;
+          if (v < nvec) {
+            float x[E];
+            unpack(dv[q][k], x, (T*)nullptr);
+#pragma unroll
+            for (int e = 0; e < E; ++e) acc[k][e] += dl[q] * x[e];
+            if (ATOMIC) {
+              float* dst = dD_acc + (drow[q] * nvec + v) * E;
+#pragma unroll
+              for (int e = 0; e < E; e += 4)
+                atomicAdd(reinterpret_cast<float4*>(dst + e),
+                          make_float4(dl[q] * qv[k][e], dl[q] * qv[k][e + 1], dl[q] * qv[k][e + 2],
+                                      dl[q] * qv[k][e + 3]));
+            }
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int v = lane + 32 * k;
+      if (v < nvec) dQ[r * nvec + v] = pack(acc[k], (T*)nullptr);
+    }
+  }
+}
+
+// Warp per destination document token: sources summed in ascending id order.
+template <typename T, int NV, bool INB>
+__global__ void __launch_bounds__(SC_WARPS * 32, 2)
+csr_scatter_vec_kernel(BwdParams b, const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col_idx) {
+  constexpr int E = V16<T>::E;
+  __shared__ int32_t seg_s[SC_WARPS][SC_SEG];
+  const ScanParams& p = b.g;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  int32_t* seg = seg_s[w];
+  const uint4* Q = static_cast<const uint4*>(p.Q);
+  uint4* dD = static_cast<uint4*>(b.dD);
+  const int nvec = p.dim / E;
+  const int64_t warp = (int64_t)blockIdx.x * SC_WARPS + w;
+  const int64_t nwarps = (int64_t)gridDim.x * SC_WARPS;
+  for (int64_t d = warp; d < b.nd_rows; d += nwarps) {
+    const int32_t a0 = row_ptr[d], n = row_ptr[d + 1] - a0;
+    const bool ranked = n <= SC_SEG;
+    if (ranked) {
+      // rank each source id by counting smaller ids (ids are distinct)
+      for (int i = lane; i < n; i += 32) {
+        const int32_t x = col_idx[a0 + i];
+        int rk = 0;
+        for (int j = 0; j < n; ++j) rk += (col_idx[a0 + j] < x) ? 1 : 0;
+        seg[rk] = x;
+      }
+      __syncwarp();
+    }
+    float acc[NV][E];
+#pragma unroll
+    for (int k = 0; k < NV; ++k)
+#pragma unroll
+      for (int e = 0; e < E; ++e) acc[k][e] = 0.f;
+    for (int i0 = 0; i0 < n; i0 += VEC_UNROLL) {
+      int64_t qrow[VEC_UNROLL];
+      float dl[VEC_UNROLL];
+#pragma unroll
+      for (int q = 0; q < VEC_UNROLL; ++q) {
+        qrow[q] = -1;
+        dl[q] = 0.f;
+        if (i0 + q < n) {
+          // source ids are int32 (the CSR stores them so): 32-bit division
+          const uint32_t s = (uint32_t)(ranked ? seg[i0 + q] : col_idx[a0 + i0 + q]);
+          const uint32_t u = s / (uint32_t)p.Tq;
+          const int t = (int)(s - u * (uint32_t)p.Tq);
+          if constexpr (INB) {
+            const int64_t qi = u / (uint32_t)p.Bd;
+            qrow[q] = qi * p.Tq + t;
+            dl[q] = unit_delta<T>(b, u, (int)qi);
+          } else {
+            const Unit U = decode_unit(p, u);
+            qrow[q] = U.q0 + t;
+            dl[q] = unit_delta<T>(b, u, U.qidx);
+          }
+        }
+      }
+      uint4 qv[VEC_UNROLL][NV];
+#pragma unroll
+      for (int q = 0; q < VEC_UNROLL; ++q)
+#pragma unroll
+        for (int k = 0; k < NV; ++k) {
+          const int v = lane + 32 * k;
+          if (qrow[q] >= 0 && v < nvec) qv[q][k] = Q[qrow[q] * nvec + v];
+        }
+#pragma unroll
+      for (int q = 0; q < VEC_UNROLL; ++q) {
+        if (qrow[q] < 0) continue;
+#pragma unroll
+        for (int k = 0; k < NV; ++k) {
+          const int v = lane + 32 * k;
+          if (v < nvec) {
+            float x[E];
+            unpack(qv[q][k], x, (T*)nullptr);
+#pragma unroll
+            for (int e = 0; e < E; ++e) acc[k][e] += dl[q] * x[e];
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int v = lane + 32 * k;
+      if (v < nvec) dD[d * nvec + v] = pack(acc[k], (T*)nullptr);
+    }
+    __syncwarp();
+  }
+}
+
+// 16-byte vectors per lane for a row of `dim` elements of T, or 0 when the
+// vector paths do not apply (dim not a whole number of vectors, misaligned
+// base pointers, rows over 32 * 5 vectors, or T = double).
+template <typename T>
+static int vec_lanes(const BwdParams& b) {
+  if (sizeof(T) == 8) return 0;
+  constexpr int E = V16<T>::E;
+  const ScanParams& p = b.g;
+  if (p.dim % E != 0) return 0;
+  const uintptr_t m = reinterpret_cast<uintptr_t>(p.Q) | reinterpret_cast<uintptr_t>(p.D) |
+                      reinterpret_cast<uintptr_t>(b.dQ) | reinterpret_cast<uintptr_t>(b.dD);
+  if (m & 15) return 0;
+  const int nvec = p.dim / E;
+  const int nv = (nvec + 31) / 32;
+  return nv <= 5 ? nv : 0;  // wider rows keep the scalar kernels (register budget)
+}
+
+// Launch the vector gather / scatter when vec_lanes() allows; false otherwise.
+template <typename T, bool ATOMIC>
+static bool launch_gather_vec(const BwdParams& b, float* acc, unsigned grid, cudaStream_t s) {
+  if constexpr (sizeof(T) == 8) {
+    return false;
+  } else {
+  switch (vec_lanes<T>(b)) {
+#define FMS_GV(NV)                                                                           \
+  case NV:                                                                                   \
+    if (b.g.layout == L_INBATCH) bwd_gather_vec_kernel<T, ATOMIC, NV, true><<<grid, 256, 0, s>>>(b, acc); \
+    else bwd_gather_vec_kernel<T, ATOMIC, NV, false><<<grid, 256, 0, s>>>(b, acc);           \
+    return true;
+    FMS_GV(1) FMS_GV(2) FMS_GV(3) FMS_GV(4) FMS_GV(5)
+#undef FMS_GV
+    default: return false;
+  }
+  }
+}
+template <typename T>
+static bool launch_scatter_vec(const BwdParams& b, const int32_t* row_ptr, const int32_t* col_idx, unsigned grid,
+                               cudaStream_t s) {
+  if constexpr (sizeof(T) == 8) {
+    return false;
+  } else {
+  switch (vec_lanes<T>(b)) {
+#define FMS_SV(NV)                                                                                   \
+  case NV:                                                                                           \
+    if (b.g.layout == L_INBATCH)                                                                     \
+      csr_scatter_vec_kernel<T, NV, true><<<grid, SC_WARPS * 32, 0, s>>>(b, row_ptr, col_idx);      \
+    else                                                                                             \
+      csr_scatter_vec_kernel<T, NV, false><<<grid, SC_WARPS * 32, 0, s>>>(b, row_ptr, col_idx);     \
+    return true;
+    FMS_SV(1) FMS_SV(2) FMS_SV(3) FMS_SV(4) FMS_SV(5)
+#undef FMS_SV
+    default: return false;
+  }
+  }
+}
+
 static inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 size_t bwd_workspace_bytes(int strategy, int dtype, int64_t n_src, int64_t n_dest,
@@ -324,7 +623,8 @@ static cudaError_t run_backward(int strategy, const BwdParams& b, void* ws, size
     }
     e = cudaMemsetAsync(acc, 0, (size_t)b.nd_rows * dim * sizeof(A), s);
     if (e != cudaSuccess) return e;
-    bwd_gather_kernel<T, true><<<grid_for(b.nq_rows, 8), 256, 0, s>>>(b, acc);
+    if (!launch_gather_vec<T, true>(b, reinterpret_cast<float*>(acc), grid_for(b.nq_rows, 8), s))
+      bwd_gather_kernel<T, true><<<grid_for(b.nq_rows, 8), 256, 0, s>>>(b, acc);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     if (!wide) {
       int64_t n = b.nd_rows * dim;
@@ -350,7 +650,8 @@ static cudaError_t run_backward(int strategy, const BwdParams& b, void* ws, size
   int32_t* sums = reinterpret_cast<int32_t*>(w);
 
   // dQ gather (no atomics)
-  bwd_gather_kernel<T, false><<<grid_for(b.nq_rows, 8), 256, 0, s>>>(b, nullptr);
+  if (!launch_gather_vec<T, false>(b, nullptr, grid_for(b.nq_rows, 8), s))
+    bwd_gather_kernel<T, false><<<grid_for(b.nq_rows, 8), 256, 0, s>>>(b, nullptr);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   // counting sort: counts land at row_ptr[dest], exclusive scan turns them into
   // segment starts, row_ptr[n_dest] = nnz.
@@ -370,7 +671,8 @@ static cudaError_t run_backward(int strategy, const BwdParams& b, void* ws, size
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   if (n_dest > 0) {
-    csr_scatter_kernel<T><<<grid_for(n_dest, SC_WARPS), SC_WARPS * 32, 0, s>>>(b, row_ptr, col_idx);
+    if (!launch_scatter_vec<T>(b, row_ptr, col_idx, grid_for(n_dest, SC_WARPS), s))
+      csr_scatter_kernel<T><<<grid_for(n_dest, SC_WARPS), SC_WARPS * 32, 0, s>>>(b, row_ptr, col_idx);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   return cudaSuccess;

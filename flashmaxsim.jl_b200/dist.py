@@ -8,7 +8,11 @@ single-device; these paths are new.  Only small outputs cross NVLink:
   * INT8 exhaustive search: every rank keeps its local top-k per query, the
     (nq, k) lists are all-gathered and merged on the device;
   * packed scan: contiguous doc ranges per rank, all-gather of the (nq, B_r)
-    score blocks.
+    score blocks;
+  * in-batch training: documents sharded (contiguous ranges of Bd), queries
+    replicated; the forward all-gathers the (Bq, Bd_r) score blocks into S,
+    the backward keeps dD local and all-reduces the dQ partial sums (in
+    float32, then one rounding to T).
 
 The merge functions take the local results as tensors and are independent of
 the kernels, so their host logic is tested with gloo ranks on CPU.
@@ -119,3 +123,80 @@ def gather_packed_scores(S_local, counts, group=None):
     parts = [torch.empty_like(buf) for _ in range(world)]
     dist.all_gather(parts, buf, group=group)
     return torch.cat([p[:, :c] for p, c in zip(parts, counts)], dim=1)
+
+
+def _local_inbatch_forward(Q, D_local, qmask, dmask_local, normalize):
+    """Scores and argmax tape of this rank's documents (fms_inbatch_fwd)."""
+    return L.inbatch_forward(Q, D_local, qmask, dmask_local, normalize, want_args=True)
+
+
+def _local_inbatch_pullback(g_local, Q, D_local, qmask, tape, inv_n, strategy):
+    """dQ partial and dD of this rank's documents (fms_inbatch_bwd)."""
+    return L.inbatch_pullback(g_local, Q, D_local, qmask, tape, inv_n, strategy)
+
+
+def _inv_counts(qmask, Q):
+    """inv_n = T(1 / max(sum(qmask), 1)) per query (normalize.jl:4-24): the
+    reciprocal in the accumulate type (float64 for Float64, else float32),
+    rounded to T, as fms_inv_counts computes it."""
+    Bq, Tq = Q.shape[0], Q.shape[1]
+    acc = torch.float64 if Q.dtype == torch.float64 else torch.float32
+    if qmask is None:
+        n = torch.full((Bq,), float(Tq), dtype=acc, device=Q.device)
+    else:
+        n = qmask.to(acc).sum(dim=1)
+    return (1.0 / torch.clamp(n, min=1.0)).to(Q.dtype)
+
+
+class _ShardedInBatch(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, Q, D_local, qmask, dmask_local, cfg, counts, group, fwd, pullback):
+        S_local, tape = fwd(Q, D_local, qmask, dmask_local, cfg.normalize)
+        world = dist.get_world_size(group) if dist.is_initialized() else 1
+        rank = dist.get_rank(group) if world > 1 else 0
+        S = gather_packed_scores(S_local.contiguous(), counts, group)
+        ctx.cfg, ctx.group, ctx.pullback = cfg, group, pullback
+        ctx.off = sum(counts[:rank])
+        ctx.save_for_backward(Q, D_local, qmask, tape)
+        return S
+
+    @staticmethod
+    def backward(ctx, gS):
+        Q, D_local, qmask, tape = ctx.saved_tensors
+        n = D_local.shape[0]
+        g_local = gS[:, ctx.off:ctx.off + n].contiguous()
+        inv = _inv_counts(qmask, Q) if ctx.cfg.normalize else None
+        dQ, dD = ctx.pullback(g_local, Q, D_local, qmask, tape, inv, ctx.cfg.backward)
+        if dist.is_initialized() and dist.get_world_size(ctx.group) > 1:
+            acc = dQ.to(torch.float64 if dQ.dtype == torch.float64 else torch.float32)
+            dist.all_reduce(acc, op=dist.ReduceOp.SUM, group=ctx.group)
+            dQ = acc.to(Q.dtype)
+        return dQ, dD, None, None, None, None, None, None, None
+
+
+def sharded_inbatch(Q, D_local, qmask=None, dmask_local=None, cfg=None, counts=None, group=None,
+                    local_forward=_local_inbatch_forward, local_pullback=_local_inbatch_pullback):
+    """maxsim(Q, D, InBatch()) with the Bd documents split over the group in
+    contiguous ranges (rank r holds `counts[r]` documents, in rank order).
+
+    Returns the full (Bq, Bd) score matrix on every rank; differentiable: the
+    gradient of D_local is this rank's rows of dD, the gradient of Q is the sum
+    of the ranks' partial dQ (all-reduced in float32, then rounded to T once).
+    `local_forward` / `local_pullback` compute one shard (the CUDA kernels by
+    default; tests substitute CPU restatements)."""
+    from .api import MaxSim
+    cfg = cfg or MaxSim(Q.dtype)
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    rank = dist.get_rank(group) if world > 1 else 0
+    if counts is None:
+        mine = torch.tensor([D_local.shape[0]], dtype=torch.int64, device=D_local.device)
+        sizes = [torch.zeros_like(mine) for _ in range(world)]
+        if world > 1:
+            dist.all_gather(sizes, mine, group=group)
+        else:
+            sizes = [mine]
+        counts = [int(x.item()) for x in sizes]
+    if len(counts) != world or D_local.shape[0] != counts[rank]:
+        raise DimensionMismatch("D_local rows do not match counts[rank]")
+    return _ShardedInBatch.apply(Q, D_local, qmask, dmask_local, cfg, counts, group,
+                                 local_forward, local_pullback)

@@ -119,6 +119,78 @@ def test_sharded_merges_two_gloo_ranks():
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
 
 
+def _oracle_fwd(Q, D, qm, dm, normalize):
+    import oracle as O
+    S, args = O.inbatch(Q, D, None if qm is None else qm, None if dm is None else dm,
+                        normalize=normalize)
+    return torch.from_numpy(S), torch.from_numpy(args)
+
+
+def _oracle_pullback(g, Q, D, qm, args, inv, strategy):
+    import oracle as O
+    dQ, dD = O.inbatch_pullback(g, inv, Q, D, qm, args, strategy.code)
+    return torch.from_numpy(dQ), torch.from_numpy(dD)
+
+
+def _rank_inbatch(rank, port, errq):
+    """Sharded in-batch training step == the single-device oracle step."""
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=WORLD)
+        g = torch.Generator().manual_seed(11)
+        Bq, Bd, Tq, Td, dim = 5, 7, 6, 9, 16
+        Q = torch.nn.functional.normalize(torch.randn((Bq, Tq, dim), generator=g), dim=-1)
+        D = torch.nn.functional.normalize(torch.randn((Bd, Td, dim), generator=g), dim=-1)
+        qm = torch.rand((Bq, Tq), generator=g) > 0.2
+        dm = torch.rand((Bd, Td), generator=g) > 0.3
+        gS = torch.randn((Bq, Bd), generator=g)
+        counts = [3, 4]  # unequal shards
+        lo = sum(counts[:rank])
+        for normalize in (False, True):
+            for strat in (fms.AtomicUnified(), fms.InvGrid()):
+                cfg = fms.MaxSim(torch.float32, normalize=normalize, backward=strat)
+                Qr = Q.clone().requires_grad_()
+                Dr = D[lo:lo + counts[rank]].clone().requires_grad_()
+                S = fdist.sharded_inbatch(Qr, Dr, qm, dm[lo:lo + counts[rank]], cfg=cfg,
+                                          local_forward=_oracle_fwd,
+                                          local_pullback=_oracle_pullback)
+                S.backward(gS)
+                Sw, args = _oracle_fwd(Q, D, qm, dm, normalize)
+                inv = fdist._inv_counts(qm, Q) if normalize else None
+                dQw, dDw = _oracle_pullback(gS, Q, D, qm, args, inv, strat)
+                assert torch.equal(S.detach(), Sw), (normalize, strat)
+                assert torch.allclose(Qr.grad, dQw, rtol=1e-5, atol=1e-6), (normalize, strat)
+                assert torch.equal(Dr.grad, dDw[lo:lo + counts[rank]]), (normalize, strat)
+        # counts discovered by an all-gather when not given
+        S = fdist.sharded_inbatch(Q, D[lo:lo + counts[rank]], qm, dm[lo:lo + counts[rank]],
+                                  local_forward=_oracle_fwd, local_pullback=_oracle_pullback)
+        assert torch.equal(S, _oracle_fwd(Q, D, qm, dm, False)[0])
+        dist.barrier()
+        dist.destroy_process_group()
+    except BaseException as e:
+        errq.put(f"rank {rank}: {type(e).__name__}: {e}")
+        raise
+
+
+def test_sharded_inbatch_training_two_gloo_ranks():
+    ctx = mp.get_context("spawn")
+    errq = ctx.SimpleQueue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_inbatch, args=(r, port, errq)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    msgs = []
+    while not errq.empty():
+        msgs.append(errq.get())
+    assert not msgs, msgs
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+
+
 def test_single_process_merges_are_identity():
     assert not dist.is_initialized()
     v = torch.randn(2, 3)

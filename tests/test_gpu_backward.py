@@ -147,3 +147,26 @@ def test_golden_backward(fms):
         dQ, dD = fms.paired_pullback(Dl, Q, D, qm, args, None, strategy(fms, code))
         close(dQ, g[f"dQ_{sfx}"], 1e-5, "golden dQ")
         close(dD, g[f"dD_{sfx}"], 1e-5, "golden dD")
+
+
+@pytest.mark.parametrize("code,name", MODES)
+@pytest.mark.parametrize("dim", [768, 1304, 2048])
+def test_inbatch_pullback_wide_rows(fms, oracle, code, name, dim):
+    """c3-shaped rows: dim 768 takes the 16-byte vector kernels (96 vectors,
+    three per lane); 1304 (163 vectors) and 2048 (256) need more than five per
+    lane and run the scalar kernels.  InvGrid results repeat bit for bit."""
+    rng = seeded(47)
+    Bq, Bd, Tq, Td = 6, 9, 32, 45
+    dtype = torch.bfloat16
+    Q, D = feats(rng, (Bq, Tq, dim), dtype), feats(rng, (Bd, Td, dim), dtype)
+    lens = rng.integers(8, Td + 1, Bd)
+    dm = torch.from_numpy(np.arange(Td)[None, :] < lens[:, None]).cuda()
+    _, args = fms.inbatch_forward(Q, D, None, dm)
+    Delta = torch.randn(Bq, Bd, device="cuda")
+    dQ, dD = fms.inbatch_pullback(Delta, Q, D, None, args, None, strategy(fms, code))
+    dQo, dDo = oracle.inbatch_pullback(Delta.to(dtype), None, Q, D, None, args.cpu(), code, 2)
+    close(dQ, dQo, 1e-2, f"dQ {name}")
+    close(dD, dDo, 1e-2, f"dD {name}")
+    if code == 1:
+        dQ2, dD2 = fms.inbatch_pullback(Delta, Q, D, None, args, None, strategy(fms, code))
+        assert torch.equal(dD, dD2) and torch.equal(dQ, dQ2)
