@@ -223,14 +223,18 @@ def run_c1(args, world, rank, local, dev, fms):
 BQ3, BD3, TQ3, TD3, DIM3 = 256, 256, 32, 180, 768
 
 
-def c3_inputs(dev):
+def c3_inputs(dev, world=1, rank=0):
+    """Queries and dS are global (same on every rank); rank r holds documents
+    [256 r, 256 (r + 1)) of a 256 * world document batch."""
     g = torch.Generator(device=dev)
     g.manual_seed(33)
     Q = l2n(torch.randn(BQ3, TQ3, DIM3, generator=g, device=dev)).to(torch.bfloat16)
-    D = l2n(torch.randn(BD3, TD3, DIM3, generator=g, device=dev)).to(torch.bfloat16)
-    lens = torch.randint(32, TD3 + 1, (BD3,), generator=g, device=dev)
+    dS = torch.randn(BQ3, BD3 * world, generator=g, device=dev)
+    gd = torch.Generator(device=dev)
+    gd.manual_seed(34 + rank)
+    D = l2n(torch.randn(BD3, TD3, DIM3, generator=gd, device=dev)).to(torch.bfloat16)
+    lens = torch.randint(32, TD3 + 1, (BD3,), generator=gd, device=dev)
     dmask = torch.arange(TD3, device=dev)[None, :] < lens[:, None]
-    dS = torch.randn(BQ3, BD3, generator=g, device=dev)
     return Q, D, dmask, lens, dS
 
 
@@ -243,6 +247,8 @@ def c3_config(world, lens_sum):
 
 
 def run_c3(args, world, rank, local, dev, fms):
+    if world > 1 and args.impl != "reference":
+        return run_c3_sharded(args, world, rank, local, dev, fms)
     Q, D, dmask, lens, dS = c3_inputs(dev)
     Lsum = int(lens.sum().item())
     cfg = c3_config(world, Lsum)
@@ -344,6 +350,53 @@ def run_c3(args, world, rank, local, dev, fms):
                                 "sample": f"{nsq} of 256 queries x all 256 docs (fwd + InvGrid "
                                           f"bwd, f32 on bf16-rounded inputs), {reps} repetitions, "
                                           f"scaled to 256 queries"}
+    if rank == 0:
+        print(json.dumps(line))
+
+
+def run_c3_sharded(args, world, rank, local, dev, fms):
+    """N GPUs: every rank holds 256 documents of a 256 N document batch (weak
+    scaling) and all 256 queries; one step = forward (all-gather of the
+    (256, 256) score blocks) + InvGrid backward (all-reduce of dQ)."""
+    from flashmaxsim_b200 import dist as fdist
+    import torch.distributed as dist
+    Q, D, dmask, lens, dS = c3_inputs(dev, world, rank)
+    cfgm = fms.MaxSim(torch.bfloat16, backward=fms.InvGrid())
+    counts = [BD3] * world
+
+    def step(mark):
+        q = Q.detach().requires_grad_()
+        d = D.detach().requires_grad_()
+        S = fdist.sharded_inbatch(q, d, None, dmask, cfg=cfgm, counts=counts)
+        mark("fwd")
+        S.backward(dS)
+        mark("bwd")
+
+    tm = Timer(dev, flush=True)
+    tm.run(step, max(3, args.warmup))
+    dist.barrier()
+    clocks = B.ClockSampler(local)
+    clocks.start()
+    ms, parts = tm.run(step, args.steps)
+    clk = clocks.stop()
+    ms = max_over_ranks(ms, world, dev)
+    ms_step = ms / args.steps
+    lsum = torch.tensor([float(lens.sum().item())], dtype=torch.float64, device=dev)
+    dist.all_reduce(lsum)
+    cfg = c3_config(world, int(lsum.item()))
+    cfg["workload"] = (f"c3 in-batch bf16 training step, documents sharded: Bq=256 (replicated), "
+                       f"Bd=256 per GPU x {world}, Tq 32, Td 180 (valid U[32,180]), dim 768")
+    cfg["parallelism"] = (f"documents sharded over {world} GPUs; NCCL all-gather of score blocks, "
+                          "all-reduce(sum) of dQ in float32")
+    line = base_line(args, world, "in-batch fwd+bwd steps/sec", args.steps / (ms / 1e3), "steps/s",
+                     ms_step, "bf16", cfg, scaling="weak")
+    line["gpu_launches"] = None
+    line["roofline"] = {"bound": "tensor", "note": "per-rank forward as in the 1-GPU line",
+                        "fwd_ms": parts.get("fwd", 0) / args.steps,
+                        "bwd_ms": parts.get("bwd", 0) / args.steps}
+    line["e2e"] = {"value": None, "unit": "steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0,
+                   "note": "multi-GPU c3 is measured device-resident only"}
+    line["clocks"] = clk
     if rank == 0:
         print(json.dumps(line))
 
