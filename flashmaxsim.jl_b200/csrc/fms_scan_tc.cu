@@ -23,6 +23,9 @@
 //           index, CSR bounds, first / last valid document token, document and
 //           query mask bits) into a 16-entry shared-memory metadata ring, so the
 //           dependent index -> mask global loads are off the other roles' paths;
+//           single-query units with nothing to scan (slots outside 1:N or outside
+//           this shard, empty documents) get their outputs written here and are
+//           not queued; an end marker closes the queue;
 //   warp 0  TMA producer: loads the document rows of a chunk (128/64/32/16-row
 //           boxes, stopping at the last valid token, so masked padding is not
 //           read) into an S-stage ring, with the query tile either resident
@@ -305,11 +308,13 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     // ------------------------------------------------------------ scheduler
     int have_prev = 0;       // warp-uniform: last working unit's query run
     int64_t prev_q = -1;
+    int64_t qn = 0;          // warp-uniform: units queued so far
+    float* scores_out = static_cast<float*>(p.scores);
     for (int64_t i0 = 0; i0 < my_units; i0 += 32) {
       if (__any_sync(0xffffffffu, abort_s != 0)) break;  // warp-uniform exit
       const int64_t i = i0 + lane;
       UnitMeta m;
-      int working = 0;
+      int working = 0, direct = 0;
       if (i < my_units) {
         const TcUnit U = tc_decode(P, u_begin + i);
         m.q_row0 = U.q_row0; m.d_row0 = U.d_row0;
@@ -342,6 +347,15 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         m.first = first;
         m.leff = last + 1;
         working = (m.valid && rows > 0 && m.leff > 0) ? 1 : 0;
+        if (!working && U.nq == 1) {
+          // nothing to scan (a slot outside 1:N or this shard, an empty or
+          // fully masked document, no query rows): the unit's outputs are
+          // written here and it never enters the pipeline
+          scores_out[U.out0] = U.valid ? 0.f : (float)p.neg;
+          if (ARGS)
+            for (int t = 0; t < U.arg_rows; ++t) p.args[U.arg0 + t] = 0;
+          direct = 1;
+        }
       }
       // a new query tile is needed when a working unit's query run differs from
       // the previous working unit's (scanned in unit order across the warp)
@@ -356,31 +370,44 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         }
       }
       m.aflags = anew;
-      const int64_t nb = (my_units - i0) < 32 ? (my_units - i0) : 32;
-      for (int k = 0; k < nb; ++k) {
+      // queue the other units in order (entry index qn counts queued units)
+      uint32_t enq = __ballot_sync(0xffffffffu, i < my_units && !direct);
+      while (enq) {
+        const int k = __ffs(enq) - 1;
+        enq &= enq - 1;
         if (lane == k) {
-          const int64_t idx = i0 + k;
-          const int slot = (int)(idx % UQ);
-          const uint32_t par = (uint32_t)((idx / UQ) & 1);
+          const int slot = (int)(qn % UQ);
+          const uint32_t par = (uint32_t)((qn / UQ) & 1);
           if (ptx::mbar_wait(&metae_bar[slot], par ^ 1, &abort_s)) {
             meta[slot] = m;
             ptx::mbar_arrive(&metaf_bar[slot]);
           }
         }
+        ++qn;
         __syncwarp();
         if (__any_sync(0xffffffffu, abort_s != 0)) break;
       }
     }
+    // end marker: the other roles stop at an entry with valid < 0
+    if (lane == 0 && !abort_s) {
+      const int slot = (int)(qn % UQ);
+      if (ptx::mbar_wait(&metae_bar[slot], (uint32_t)(((qn / UQ) & 1) ^ 1), &abort_s)) {
+        meta[slot].valid = -1;
+        ptx::mbar_arrive(&metaf_bar[slot]);
+      }
+    }
+    __syncwarp();
   } else if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     int stage = 0;
     uint32_t phase = 0;
     int aslot = ARES - 1;    // ARES: slot of the current query tile
     uint32_t aphase = 1;     // flips when aslot wraps to 0
-    for (int64_t i = 0; i < my_units; ++i) {
+    for (int64_t i = 0;; ++i) {  // queued units, up to the end marker
       const int slot = (int)(i % UQ);
       if (!ptx::warp_wait(&metaf_bar[slot], (uint32_t)((i / UQ) & 1), &abort_s)) goto done;
       const UnitMeta& m = meta[slot];
+      if (m.valid < 0) break;
       const int rows = m.nq * m.Tq;
       const int nmt = (rows + M - 1) / M;
       const int nch = (m.valid && rows > 0) ? (m.leff + NT - 1) / NT : 0;
@@ -448,10 +475,11 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     int aslot = ARES - 1;
     uint32_t aslot_phase = 1;
     bool holding = false;    // ARES: an A slot is in use (released on the next switch)
-    for (int64_t i = 0; i < my_units; ++i) {
+    for (int64_t i = 0;; ++i) {  // queued units, up to the end marker
       const int slot = (int)(i % UQ);
       if (!ptx::warp_wait(&metaf_bar[slot], (uint32_t)((i / UQ) & 1), &abort_s)) goto done;
       const UnitMeta& m = meta[slot];
+      if (m.valid < 0) break;
       const int rows = m.nq * m.Tq;
       const int nmt = (rows + M - 1) / M;
       const int nch = (m.valid && rows > 0) ? (m.leff + NT - 1) / NT : 0;
@@ -515,10 +543,11 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     uint32_t aphase = 0;
     uint32_t ephase = 0;
     float* scores = static_cast<float*>(p.scores);
-    for (int64_t i = 0; i < my_units; ++i) {
+    for (int64_t i = 0;; ++i) {  // queued units, up to the end marker
       const int slot = (int)(i % UQ);
       if (!ptx::warp_wait(&metaf_bar[slot], (uint32_t)((i / UQ) & 1), &abort_s)) goto done;
       const UnitMeta& m = meta[slot];
+      if (m.valid < 0) break;
       const int ub = (int)(i & 1);  // buffer of this unit (red_s, half_*)
       if (!m.valid) {
         if (et == 0) scores[m.out0] = (float)p.neg;
