@@ -17,7 +17,8 @@
 //
 // Persistent CTAs walk contiguous ranges of units (one query run x one document
 // run; the query tile then changes rarely along a CTA's range); a unit may
-// stack several queries (in-batch, multi-query packed) so one document tile
+// stack several queries (in-batch, multi-query packed; up to 256 rows in two
+// tiles and at most 128 queries) so one document tile
 // feeds all of them.  Warp roles (224 threads):
 //   warp 6  scheduler: decodes 32 upcoming units at once (one per lane: candidate
 //           index, CSR bounds, first / last valid document token, document and
@@ -204,12 +205,14 @@ struct Cfg {
   static constexpr int B_BYTES = NT * ROWB;         // one K block of a chunk
   static constexpr int ACC_COLS = MAXMT * NT;       // TMEM columns per accumulator buffer
   static constexpr int TMEM_COLS = NACC * ACC_COLS;
+  // allocation: a power of two of at least 32 columns (three 128-column tiles use 512)
+  static constexpr int TMEM_ALLOC = TMEM_COLS <= 128 ? 128 : TMEM_COLS <= 256 ? 256 : 512;
   static constexpr int HALF = NT / R;               // columns per epilogue thread per chunk
   static __host__ __device__ int stage_bytes(int KB) { return ARES ? KB * B_BYTES : A_BYTES + B_BYTES; }
   static __host__ __device__ int aslot_bytes(int KB) { return ARES ? KB * A_BYTES : 0; }
   static_assert(R == 1 || (R == 2 && M == 64 && MAXMT == 1) || (R == 4 && M == 128 && MAXMT == 1),
                 "replication: 2 copies of 32 rows in a 64-row tile, or 4 in a 128-row tile");
-  static_assert(TMEM_COLS == 128 || TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM columns");
+  static_assert(TMEM_COLS % 128 == 0 && TMEM_COLS <= 512, "TMEM columns");
   static_assert(HALF % 32 == 0, "epilogue reads 32-column groups");
 };
 
@@ -292,7 +295,7 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     ptx::prefetch_tmap(&bm.b32);
     ptx::prefetch_tmap(&bm.b16);
   }
-  if (warp == 1) ptx::tmem_alloc(&tmem_base_s, L::TMEM_COLS);
+  if (warp == 1) ptx::tmem_alloc(&tmem_base_s, L::TMEM_ALLOC);
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
@@ -751,7 +754,7 @@ done:
   __syncthreads();
   if (warp == 1) {
     ptx::tc_fence_after();
-    ptx::tmem_dealloc(tmem_base, L::TMEM_COLS);
+    ptx::tmem_dealloc(tmem_base, L::TMEM_ALLOC);
   }
 }
 
@@ -794,14 +797,16 @@ static int queries_total(const ScanParams& p) {
   return p.layout == L_INBATCH ? p.Bq : (p.layout == L_PACKED ? p.nq : 1);
 }
 
-// Queries stacked per unit and the resulting row count.
+// Queries stacked per unit and the resulting row count (up to 256 rows in two
+// 128-row tiles; at most 128 queries, one epilogue thread sums each).
 static void plan(const ScanParams& p, int& G, int& rows) {
   const int Tq = p.Tq;
   G = 1;
   if ((p.layout == L_INBATCH || p.layout == L_PACKED) && Tq > 0) {
+    const int nq = queries_total(p);
     G = 256 / Tq;
     if (G < 1) G = 1;
-    const int nq = queries_total(p);
+    if (G > 128) G = 128;
     if (G > nq) G = nq > 0 ? nq : 1;
   }
   rows = G * Tq;

@@ -89,3 +89,42 @@ def test_paired_row_configs(fms, oracle, Tq, Td):
     assert_scores(s.cpu(), so, 1e-3)
     Qc, Dc = Q.cpu(), D.cpu()
     assert_args(a.cpu(), ao, lambda i, u: sims(Qc[i[0]], Dc[i[0]])[i[1], u - 1], 1e-3)
+
+
+@pytest.mark.parametrize("nq,Tq", [(16, 24), (40, 24), (13, 30)])
+def test_packed_query_groups(fms, oracle, nq, Tq):
+    """Packed scans whose stacked queries exceed one unit's 256 rows run in
+    several query groups (the last one partial); query masks, a fully masked
+    query and normalisation included."""
+    g = torch.Generator().manual_seed(nq * Tq)
+    dim = 128
+    lens = torch.randint(1, 400, (23,), generator=g).tolist()
+    lens[5] = 0
+    docs = [l2t(torch.randn(n, dim, generator=g)).half().cuda() for n in lens]
+    P = fms.pack_docs(docs)
+    Qs = l2t(torch.randn(nq, Tq, dim, generator=g)).half().cuda()
+    qm = torch.rand(nq, Tq, generator=g) > 0.2
+    qm[2] = False
+    for normalize in (False, True):
+        S, A = fms.packed_forward(Qs, P, qm.cuda(), normalize=normalize)
+        So, Ao = oracle.packed(Qs, P.tokens, P.cu.cpu(), qm, normalize=normalize)
+        assert_scores(S.cpu(), So, 1e-3)
+        Qc, tok, cu = Qs.cpu(), P.tokens.cpu(), P.cu.cpu().numpy()
+        assert_args(A.cpu(), Ao,
+                    lambda i, u: sims(Qc[i[0]], tok[cu[i[1]] - 1:cu[i[1] + 1] - 1])[i[2], u - 1], 1e-3)
+
+
+def test_stacked_single_token_queries(fms, oracle):
+    """Tq = 1: at most 128 queries are stacked per unit (one epilogue thread sums
+    each), so 300 single-token queries run in three groups."""
+    g = torch.Generator().manual_seed(77)
+    Bq, Bd, Td, dim = 300, 7, 50, 64
+    Q = l2t(torch.randn(Bq, 1, dim, generator=g)).half().cuda()
+    D = l2t(torch.randn(Bd, Td, dim, generator=g)).half().cuda()
+    S, A = fms.inbatch_forward(Q, D)
+    So, Ao = oracle.inbatch(Q, D)
+    assert_scores(S.cpu(), So, 1e-3)
+    docs = [D[j] for j in range(Bd)]
+    P = fms.pack_docs(docs)
+    S2, _ = fms.packed_forward(Q, P)
+    assert_scores(S2.cpu(), So, 1e-3)
