@@ -54,6 +54,7 @@ def parse():
     # the other BASELINE.json configs (measured one at a time; the default line is c2)
     ap.add_argument("--workload", default="c2", choices=["c1", "c2", "c3", "c4", "c5"])
     ap.add_argument("--c5-ndoc", type=int, default=0, help="smaller c5 index (profiling)")
+    ap.add_argument("--c4-ndoc", type=int, default=0, help="smaller c4 gallery (profiling)")
     return ap.parse_args()
 
 

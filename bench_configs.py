@@ -406,15 +406,15 @@ def run_c3_sharded(args, world, rank, local, dev, fms):
 NQ4, TQ4, DIM4, NDOC4 = 16, 24, 128, 50_000
 
 
-def c4_inputs(dev, fms, world, rank):
+def c4_inputs(dev, fms, world, rank, ndoc=NDOC4):
     g = torch.Generator(device=dev)
     g.manual_seed(44)
-    lens = torch.randint(700, 1031, (NDOC4,), generator=g, device=dev)
+    lens = torch.randint(700, 1031, (ndoc,), generator=g, device=dev)
     gq = torch.Generator(device=dev)
     gq.manual_seed(45)
     Qs = l2n(torch.randn(NQ4, TQ4, DIM4, generator=gq, device=dev)).half()
-    lo = NDOC4 * rank // world
-    hi = NDOC4 * (rank + 1) // world
+    lo = ndoc * rank // world
+    hi = ndoc * (rank + 1) // world
     my = lens[lo:hi]
     ntok = int(my.sum().item())
     tokens = torch.empty((ntok, DIM4), dtype=torch.float16, device=dev)
@@ -428,13 +428,14 @@ def c4_inputs(dev, fms, world, rank):
     cu[1:] = torch.cumsum(my, 0)
     cu = (cu + 1).to(torch.int32)
     P = fms.make_packed(tokens, cu)
-    counts = [NDOC4 * (r + 1) // world - NDOC4 * r // world for r in range(world)]
+    counts = [ndoc * (r + 1) // world - ndoc * r // world for r in range(world)]
     return Qs, P, ntok, counts
 
 
 def run_c4(args, world, rank, local, dev, fms):
-    Qs, P, ntok, counts = c4_inputs(dev, fms, world, rank)
-    cfg = {"workload": "c4 packed varlen scan f16: 16 q x 24 tok x 128 dim vs PackedSeq of 50000 "
+    ndoc = args.c4_ndoc or NDOC4
+    Qs, P, ntok, counts = c4_inputs(dev, fms, world, rank, ndoc)
+    cfg = {"workload": f"c4 packed varlen scan f16: 16 q x 24 tok x 128 dim vs PackedSeq of {ndoc} "
                        "docs, len U[700,1030], 1-based cu",
            "l2": "inputs larger than L2 (11 GB of tokens per step)",
            "parallelism": f"contiguous doc ranges over {world} GPU(s)" +
@@ -485,7 +486,7 @@ def run_c4(args, world, rank, local, dev, fms):
     ms_step = ms / args.steps
     value = NQ4 * tot_tok * args.steps / (ms / 1e3)
     Qh = Qs.cpu().pin_memory()
-    Sh = torch.empty((NQ4, NDOC4), dtype=torch.float32).pin_memory()
+    Sh = torch.empty((NQ4, ndoc), dtype=torch.float32).pin_memory()
 
     def e2e_step(mark):
         q = Qh.to(dev, non_blocking=True)
