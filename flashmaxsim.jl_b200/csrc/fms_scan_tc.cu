@@ -911,7 +911,9 @@ cudaError_t launch_scan_tc(int dtype, const ScanParams& p, cudaStream_t s) {
     return tc::launch_cfg<128, 256, 1, 4, 1, 2, 0>(P, a, bm, s, 2, B2);
   if (rows <= 64) return tc::launch_auto<64, 64, 1, 1, 4, 8>(P, a, bm, s, 2, B2);
   if (rows <= 128) return tc::launch_auto<128, 64, 1, 1, 4, 8>(P, a, bm, s, 2, B2);
-  return tc::launch_auto<128, 128, 2, 1, 2, 12>(P, a, bm, s, 1, B1);
+  // two 128-row tiles: two CTAs per SM, one 256-column accumulator each (two
+  // MMA issuers and epilogues per SM beat one CTA with two accumulators)
+  return tc::launch_auto<128, 128, 2, 1, 1, 12>(P, a, bm, s, 2, B2);
 }
 
 }  // namespace fms
