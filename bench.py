@@ -173,18 +173,6 @@ def arm_config(world, total_tok):
                            (", NCCL all-reduce(max) merge" if world > 1 else "")}
 
 
-def profiled_traffic():
-    """DRAM bytes per scan launch (dram__bytes_read.sum + dram__bytes_write.sum)
-    from the committed ncu summary of the full-size c2 launch, or None."""
-    p = ROOT / "profiles" / "tc_scan_c2_dram.md"
-    if not p.exists():
-        return None, None
-    for line in p.read_text().splitlines():
-        if line.startswith("traffic_bytes_per_launch:"):
-            return float(line.split(":", 1)[1].strip()), p.name
-    return None, None
-
-
 def measured_peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -193,55 +181,134 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
-def cpu_sample(Q, gallery, dmask, idxs, nq=8):
-    """Bounded sample for the CPU arm: the first `nq` queries with all their
-    candidates, gallery reduced to the referenced docs (widened to float32 as
-    the reference's dot_accum does).  Returns the oracle inputs + doc tokens."""
-    ix = idxs[:nq].cpu().numpy()
-    valid = (ix >= 1) & (ix <= NDOC)
-    uniq = np.unique(ix[valid])
-    remap = np.zeros(NDOC + 1, np.int32)
+def shard_sample(Q, gallery, dmask, idxs, lo, n_global, nq=8):
+    """A bounded sample of the c2 workload for the CPU arms and the parity check:
+    the first `nq` queries with every candidate slot; the gallery shard held here
+    (global ids lo .. lo + len(gallery) - 1) reduced to the documents those slots
+    reference (widened to float32 as the reference's dot_accum does).  Slots of
+    other shards become local id 0 (so the oracle gives them `neg`).  Returns the
+    oracle inputs, the slot classes and the sample's valid doc tokens."""
+    n_local = gallery.shape[0]
+    ix = idxs[:nq].cpu().numpy().astype(np.int64)
+    own = (ix >= lo) & (ix < lo + n_local)
+    invalid = (ix < 1) | (ix > n_global)
+    loc = ix - (lo - 1)
+    uniq = np.unique(loc[own])
+    remap = np.zeros(n_local + 1, np.int32)
     remap[uniq] = np.arange(1, len(uniq) + 1, dtype=np.int32)
-    ix_local = np.where(valid, remap[np.clip(ix, 0, NDOC)], 0).astype(np.int32)
+    ix_local = np.where(own, remap[np.clip(loc, 0, n_local)], 0).astype(np.int32)
     sel = torch.from_numpy(uniq - 1).to(gallery.device)
     G = gallery.index_select(0, sel).float().cpu().numpy()
     dm = dmask.index_select(0, sel).cpu().numpy()
     Qn = Q[:nq].float().cpu().numpy()
-    ntok = int(dm.sum(1)[ix_local[valid] - 1].sum())
-    return Qn, G, dm, ix_local, ntok
+    ntok = int(dm.sum(1)[ix_local[own] - 1].sum())
+    return {"Q": Qn, "G": G, "dm": dm, "ix": ix_local, "own": own, "invalid": invalid,
+            "ntok": ntok, "nq": nq, "loc": np.where(own, loc, 0).astype(np.int32)}
 
 
-def time_cpu(Qn, G, dm, ix, ntok, min_seconds=10.0, threads=None):
-    """Repeat the CPU pass until at least `min_seconds` of CPU work was timed."""
+def parity_c2(S, Q, gallery, dmask, idxs, lo, n_global, neg, samp, So, Ao):
+    """Parity of the timed run's scores against the oracle on the sample: max
+    relative error over the sampled slots this rank holds (tolerance 1e-3,
+    f16 in / f32 accumulate), `neg` in globally invalid slots, and the argmax
+    tape of the same slots (one untimed forward with the tape) identical to the
+    oracle's except at ties within 1e-3 (float64 similarities)."""
+    import flashmaxsim_b200 as fms
+    nq = samp["nq"]
+    Sg = S[:nq].float().cpu().numpy()
+    own, invalid = samp["own"], samp["invalid"]
+    rel = np.abs(Sg[own] - So[own]) / np.maximum(1.0, np.abs(So[own])) if own.any() else \
+        np.zeros(1)
+    neg_ok = bool(np.all(Sg[invalid] == neg)) if invalid.any() else True
+    ixl = torch.from_numpy(samp["loc"]).to(gallery.device)
+    _, A = fms.candidates_forward(Q[:nq], gallery, ixl, None, dmask, neg=neg, want_args=True)
+    A = A.cpu().numpy()
+    Gh, Qh = samp["G"], samp["Q"]
+    ties = non_tie = 0
+    for b, c, t in np.argwhere((A != Ao) & own[:, :, None]):
+        g, r = int(A[b, c, t]), int(Ao[b, c, t])
+        if g == 0 or r == 0:
+            non_tie += 1
+            continue
+        doc = Gh[samp["ix"][b, c] - 1].astype(np.float64)
+        q = Qh[b, t].astype(np.float64)
+        sg, sr = float(doc[g - 1] @ q), float(doc[r - 1] @ q)
+        if abs(sg - sr) <= 1e-3 * max(1.0, abs(sr)):
+            ties += 1
+        else:
+            non_tie += 1
+    mre = float(rel.max())
+    return {"sample": f"first {nq} queries x their {int(own.sum())} candidate slots held by this "
+                      f"rank (+{int(invalid.sum())} invalid slots), output of the last timed step",
+            "max_rel_err": mre, "tol": 1e-3, "neg_slots_ok": neg_ok,
+            "argmax_checked": int(own.sum()) * Q.shape[1], "argmax_ties": int(ties),
+            "argmax_mismatch_non_tie": int(non_tie),
+            "pass": bool(mre <= 1e-3 and neg_ok and non_tie == 0)}
+
+
+def time_cpu(samp, min_seconds=10.0, threads=None):
+    """Repeat the CPU pass until at least `min_seconds` of CPU work was timed.
+    Returns (doc-tokens/s, threads, seconds per pass, passes, (S, args) of the
+    last pass)."""
     sys.path.insert(0, str(ROOT / "oracle"))
     import oracle as O
     threads = threads or O.default_threads()
+    Qn, G, dm, ix = samp["Q"], samp["G"], samp["dm"], samp["ix"]
     O.candidates(Qn[:1], G, ix[:1], None, dm, neg=float("-inf"), nthreads=threads)  # warm
     t0 = time.perf_counter()
     reps = 0
     while True:
-        O.candidates(Qn, G, ix, None, dm, neg=float("-inf"), nthreads=threads)
+        out = O.candidates(Qn, G, ix, None, dm, neg=float("-inf"), nthreads=threads)
         reps += 1
         if time.perf_counter() - t0 >= min_seconds:
             break
     dt = (time.perf_counter() - t0) / reps
-    return ntok / dt, threads, dt, reps
+    return samp["ntok"] / dt, threads, dt, reps, out
+
+
+def reference_sample(world, dev, nq=4):
+    """The reference arm's per-step sample of the N-GPU workload: the first `nq`
+    queries with every one of their candidate slots over the whole N x 100k
+    gallery.  The gallery shards are regenerated one at a time on this device
+    (the same seeds every rank uses) and only the referenced documents are kept.
+    Returns the oracle inputs, the sample's doc tokens and the whole workload's
+    doc tokens per step (the same figure the N-GPU arm reports)."""
+    parts, total_tok = [], 0
+    for r in range(world):
+        Q, gallery, dmask, lens, idxs = make_workload(world, r, dev)
+        tok, _ = doc_tokens(idxs, lens, world, r)
+        total_tok += tok
+        samp = shard_sample(Q, gallery, dmask, idxs, r * NDOC + 1, NDOC * world, nq=nq)
+        parts.append(samp)
+        del gallery, dmask
+        torch.cuda.empty_cache()
+    # one gallery of the referenced documents of every shard; slot ids into it
+    G = np.concatenate([p["G"] for p in parts], axis=0)
+    dm = np.concatenate([p["dm"] for p in parts], axis=0)
+    ix = np.zeros_like(parts[0]["ix"])
+    base = 0
+    for p in parts:
+        ix = np.where(p["own"], p["ix"] + base, ix)
+        base += p["G"].shape[0]
+    ntok = sum(p["ntok"] for p in parts)
+    return {"Q": parts[0]["Q"], "G": G, "dm": dm, "ix": ix.astype(np.int32), "ntok": ntok}, \
+        total_tok
 
 
 def run_reference(args, world, rank):
+    """The reference's CPU algorithm (oracle port of the Array path) on all host
+    cores, on the same config the N-GPU arm runs: each step scores a bounded
+    sample of it (4 queries x all their candidates)."""
     if rank != 0:
         return
     dev = torch.device("cuda", 0) if torch.cuda.is_available() else torch.device("cpu")
     if dev.type == "cpu":
         print(json.dumps({"impl": "reference", "unavailable": "no device to build the workload"}))
         return
-    Q, gallery, dmask, lens, idxs = make_workload(1, 0, dev)
-    full_tok, _ = doc_tokens(idxs, lens, 1, 0)
-    Qn, G, dm, ix, ntok = cpu_sample(Q, gallery, dmask, idxs, nq=4)
-    del gallery
+    samp, full_tok = reference_sample(world, dev, nq=4)
     sys.path.insert(0, str(ROOT / "oracle"))
     import oracle as O
     threads = O.default_threads()
+    Qn, G, dm, ix, ntok = samp["Q"], samp["G"], samp["dm"], samp["ix"], samp["ntok"]
     for _ in range(args.warmup):
         O.candidates(Qn, G, ix, None, dm, neg=float("-inf"), nthreads=threads)
     t0 = time.perf_counter()
@@ -249,14 +316,15 @@ def run_reference(args, world, rank):
         O.candidates(Qn, G, ix, None, dm, neg=float("-inf"), nthreads=threads)
     dt = (time.perf_counter() - t0) / args.steps
     v = ntok / dt
-    sample = (f"4 of 64 queries x all 1000 candidates per step ({ntok} valid doc-tokens), "
-              f"oracle port of the reference CPU Array path, OpenMP over pairs")
+    sample = (f"4 of 64 queries x all {C * world} candidate slots per step ({ntok} valid "
+              f"doc-tokens), oracle port of the reference CPU Array path, OpenMP over pairs "
+              f"on {threads} host threads")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded randn, L2-normalised tokens)",
-        "config": arm_config(1, full_tok),
+        "config": arm_config(world, full_tok),
         "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -283,23 +351,25 @@ def main():
         return
     import flashmaxsim_b200 as fms
     from flashmaxsim_b200 import dist as fdist
+    if world > 1:
+        import torch.distributed as dist
     dev = torch.device("cuda", local)
     Q, gallery, dmask, lens, idxs = make_workload(world, rank, dev)
     ntok, nslots = doc_tokens(idxs, lens, world, rank)
     neg = float("-inf")
+    lo = rank * NDOC + 1
 
-    def step():
+    def step(mark=None):
         if world == 1:
             return fms.candidates_forward(Q, gallery, idxs, None, dmask, neg=neg,
                                           want_args=False)[0]
-        return fdist.sharded_candidates(Q, gallery, idxs, None, dmask, shard_lo=rank * NDOC + 1,
-                                        n_global=NDOC * world, neg=neg)
+        return fdist.sharded_candidates(Q, gallery, idxs, None, dmask, shard_lo=lo,
+                                        n_global=NDOC * world, neg=neg, mark=mark)
 
     for _ in range(max(3, args.warmup)):
         step()
     torch.cuda.synchronize()
     if world > 1:
-        import torch.distributed as dist
         dist.barrier()
     clocks = ClockSampler(local)
     clocks.start()
@@ -327,30 +397,52 @@ def main():
     ms_step = ms_max / args.steps
     value = total_tok * args.steps / (ms_max / 1e3)
 
+    # per-phase device time of the sharded step (separate untimed pass with events
+    # between the phases), mean per step, max over ranks
+    phases = None
+    if world > 1:
+        acc = {}
+        for _ in range(args.steps):
+            marks = []
+
+            def mark(name):
+                e = torch.cuda.Event(enable_timing=True)
+                e.record()
+                marks.append((name, e))
+            mark("start")
+            step(mark)
+            torch.cuda.synchronize()
+            for (n0, e0), (n1, e1) in zip(marks[:-1], marks[1:]):
+                acc[n1] = acc.get(n1, 0.0) + e0.elapsed_time(e1)
+        names = sorted(acc)
+        vec = torch.tensor([acc[n] / args.steps for n in names], dtype=torch.float64, device=dev)
+        dist.all_reduce(vec, op=dist.ReduceOp.MAX)
+        phases = {n: float(v) for n, v in zip(names, vec.tolist())}
+
     # e2e: through the public API with host buffers (queries + idxs in, scores out)
     Qh = Q.cpu().pin_memory()
     ih = idxs.cpu().pin_memory()
     Sh = torch.empty(S.shape, dtype=S.dtype).pin_memory()
-    for _ in range(2):
-        Sd = fms.maxsim(Qh.to(dev, non_blocking=True), gallery, ih.to(dev, non_blocking=True),
-                        None, dmask, neg=neg) if world == 1 else step()
+
+    def e2e_step():
+        Qd = Qh.to(dev, non_blocking=True)
+        idd = ih.to(dev, non_blocking=True)
+        if world == 1:
+            Sd = fms.maxsim(Qd, gallery, idd, None, dmask, neg=neg)
+        else:
+            Sd = fdist.sharded_candidates(Qd, gallery, idd, None, dmask, shard_lo=lo,
+                                          n_global=NDOC * world, neg=neg)
         Sh.copy_(Sd, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if world > 1:
         dist.barrier()
     e0.record()
     for _ in range(args.steps):
-        if world == 1:
-            Sd = fms.maxsim(Qh.to(dev, non_blocking=True), gallery,
-                            ih.to(dev, non_blocking=True), None, dmask, neg=neg)
-        else:
-            Qd = Qh.to(dev, non_blocking=True)
-            idd = ih.to(dev, non_blocking=True)
-            Sd = fdist.sharded_candidates(Qd, gallery, idd, None, dmask,
-                                          shard_lo=rank * NDOC + 1, n_global=NDOC * world,
-                                          neg=neg)
-        Sh.copy_(Sd, non_blocking=True)
+        e2e_step()
     e1.record()
     torch.cuda.synchronize()
     te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
@@ -360,12 +452,13 @@ def main():
     h2d = Qh.numel() * Qh.element_size() + ih.numel() * ih.element_size()
     d2h = Sh.numel() * Sh.element_size()
 
-    # roofline of the scan kernel (single launch per step at N=1)
+    # roofline of the scan kernel: algorithmic bytes = valid doc rows + their
+    # masks + the queries + idxs read and the scores written
     alg_bytes = ntok * DIM * 2 + nslots * TD + Q.numel() * 2 + idxs.numel() * 4 + \
         idxs.numel() * 4
     peak, peak_kind = measured_peaks()
-    achieved = alg_bytes / (ms_step / 1e3) / 1e9
-    traffic, traffic_src = profiled_traffic() if world == 1 else (None, None)
+    scan_ms = phases["scan"] if phases else ms_step
+    achieved = alg_bytes / (scan_ms / 1e3) / 1e9
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
@@ -375,25 +468,38 @@ def main():
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h,
                 "note": "gallery resident in HBM (index); queries+idxs H2D, scores D2H"},
-        "gpu_launches": args.steps * (1 if world == 1 else 2),
+        "gpu_launches": args.steps * (1 if world == 1 else 3),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "traffic": traffic,
-                     "traffic_source": traffic_src,
+                     "frac": achieved / peak, "traffic": None,
+                     "traffic_note": "DRAM bytes of the scan are in the committed ncu summaries "
+                                     "under profiles/ (separate capture, not this run)",
                      "peak_source": f"{peak_kind} hbm_gbs", "kernel": "candidates scan",
+                     "kernel_ms": scan_ms,
                      "algorithmic_bytes_per_launch": alg_bytes},
         "clocks": clk,
     }
+    if phases:
+        line["phases_ms"] = phases
+    samp = shard_sample(Q, gallery, dmask, idxs, lo, NDOC * world, nq=8) if rank == 0 else None
+    out = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        Qn, G, dm, ix, ctok = cpu_sample(Q, gallery, dmask, idxs, nq=8)
-        v, thr, dt, reps = time_cpu(Qn, G, dm, ix, ctok, min_seconds=10.0)
+        v, thr, dt, reps, out = time_cpu(samp, min_seconds=10.0)
         line["cpu_baseline"] = {
             "value": v, "unit": UNIT, "cores": thr, "kind": "port",
-            "sample": f"8 of 64 queries x all candidates ({ctok} valid doc-tokens per pass, "
-                      f"{reps} passes, {dt * reps:.1f} s), oracle C port of the reference CPU "
-                      "Array path, OpenMP over pairs"}
+            "sample": f"8 of 64 queries x all candidates ({samp['ntok']} valid doc-tokens per "
+                      f"pass, {reps} passes, {dt * reps:.1f} s), oracle C port of the reference "
+                      "CPU Array path, OpenMP over pairs"}
     if rank == 0:
+        if out is None:
+            sys.path.insert(0, str(ROOT / "oracle"))
+            import oracle as O
+            out = O.candidates(samp["Q"], samp["G"], samp["ix"], None, samp["dm"], neg=neg,
+                               nthreads=O.default_threads())
+        line["parity"] = parity_c2(S, Q, gallery, dmask, idxs, lo, NDOC * world, neg, samp,
+                                   out[0], out[1])
         print(json.dumps(line))
     if world > 1:
+        dist.barrier()
         dist.destroy_process_group()
 
 

@@ -123,6 +123,42 @@ def time_cpu(fn, min_seconds=10.0):
     return (time.perf_counter() - t0) / reps, reps
 
 
+def max_rel_err(got, ref):
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    if got.size == 0:
+        return 0.0
+    return float((np.abs(got - ref) / np.maximum(1.0, np.abs(ref))).max())
+
+
+def args_check(got, ref, sim, tol):
+    """Argmax tapes: (ties, non-tie mismatches); sim(index, u) is the float64
+    similarity of the source at `index` with doc token u (1-based)."""
+    got, ref = np.asarray(got), np.asarray(ref)
+    ties = bad = 0
+    for idx in np.argwhere(got != ref):
+        idx = tuple(idx)
+        g, r = int(got[idx]), int(ref[idx])
+        if g == 0 or r == 0:
+            bad += 1
+            continue
+        sg, sr = sim(idx, g), sim(idx, r)
+        if abs(sg - sr) <= tol * max(1.0, abs(sr)):
+            ties += 1
+        else:
+            bad += 1
+    return ties, bad
+
+
+def parity_record(sample, mre, tol, ties=0, bad=0, checked=0, **extra):
+    rec = {"sample": sample, "max_rel_err": mre, "tol": tol, "argmax_checked": checked,
+           "argmax_ties": ties, "argmax_mismatch_non_tie": bad}
+    rec.update(extra)
+    rec["pass"] = bool(mre <= tol and bad == 0 and all(v for k, v in extra.items()
+                                                        if k.endswith("_ok")))
+    return rec
+
+
 # --------------------------------------------------------------------------- c1
 
 def c1_inputs(dev):
@@ -203,6 +239,16 @@ def run_c1(args, world, rank, local, dev, fms):
                         "fwd_ms": parts.get("fwd", 0) / args.steps,
                         "bwd_ms": parts.get("bwd", 0) / args.steps}
     line["clocks"] = clk
+    if rank == 0:
+        O = oracle()
+        Qn, Dn = Q.cpu().numpy(), D.cpu().numpy()
+        S, a = fms.paired_forward(Q, D, want_args=True)
+        So, Ao = O.paired(Qn, Dn, nthreads=O.default_threads())
+        sims = np.einsum("btk,buk->btu", Qn.astype(np.float64), Dn.astype(np.float64))
+        ties, bad = args_check(a.cpu().numpy(), Ao, lambda i, u: sims[i[0], i[1], u - 1], 1e-5)
+        line["parity"] = parity_record("the whole c1 forward (32 pairs), scores and argmax tape",
+                                       max_rel_err(S.cpu().numpy(), So), 1e-5, ties, bad,
+                                       checked=int(Ao.size))
     if rank == 0 and not args.no_cpu_baseline:
         O = oracle()
         Qn, Dn = Q.cpu().numpy(), D.cpu().numpy()
@@ -246,31 +292,63 @@ def c3_config(world, lens_sum):
             "parallelism": f"replicas ({world} GPU(s))"}
 
 
+def c3_reference_inputs(dev, world):
+    """The N-GPU c3 workload on one device: the replicated queries and dS, and
+    the documents of every rank (256 per rank, their seeds), concatenated."""
+    Ds, ms, ls = [], [], []
+    for r in range(world):
+        Q, D, dmask, lens, dS = c3_inputs(dev, world, r)
+        Ds.append(D)
+        ms.append(dmask)
+        ls.append(lens)
+    return Q, torch.cat(Ds), torch.cat(ms), torch.cat(ls), dS
+
+
+def c3_cpu_step(O, Q, D, dmask, dS, nsq, thr):
+    """The oracle's c3 step on the first nsq queries x all documents: the
+    forward (f32 on the bf16-rounded inputs) and the InvGrid pullback."""
+    Qn, Dn = Q[:nsq].float().cpu().numpy(), D.float().cpu().numpy()
+    dm, dSn = dmask.cpu().numpy(), dS[:nsq].cpu().numpy()
+
+    def step():
+        S, a = O.inbatch(Qn, Dn, None, dm, nthreads=thr)
+        dQ, _ = O.inbatch_pullback(dSn, None, Qn, Dn, None, a, 1, dtype_code=2)
+        return S, a, dQ
+    return step, Qn, Dn
+
+
 def run_c3(args, world, rank, local, dev, fms):
     if world > 1 and args.impl != "reference":
         return run_c3_sharded(args, world, rank, local, dev, fms)
-    Q, D, dmask, lens, dS = c3_inputs(dev)
+    if args.impl == "reference":
+        # the same workload the N-GPU arm runs (256 documents per GPU)
+        Q, D, dmask, lens, dS = c3_reference_inputs(dev, world)
+    else:
+        Q, D, dmask, lens, dS = c3_inputs(dev)
     Lsum = int(lens.sum().item())
     cfg = c3_config(world, Lsum)
+    if world > 1:
+        cfg["workload"] = (f"c3 in-batch bf16 training step, documents sharded: Bq=256 "
+                           f"(replicated), Bd=256 per GPU x {world}, Tq 32, Td 180 (valid "
+                           f"U[32,180]), dim 768")
+    bd = D.shape[0]
     fwd_flop = 2.0 * BQ3 * TQ3 * DIM3 * Lsum
+    # backward: one multiply-add per feature element for every (query token,
+    # document) source, once for dQ and once for dD
+    bwd_flop = 2.0 * 2.0 * BQ3 * bd * TQ3 * DIM3
     if args.impl == "reference":
         O = oracle()
         thr = O.default_threads()
         nsq = 8
-        Qn, Dn = Q[:nsq].float().cpu().numpy(), D.float().cpu().numpy()
-        dm, dSn = dmask.cpu().numpy(), dS[:nsq].cpu().numpy()
-
-        def cpu_step():
-            S, a = O.inbatch(Qn, Dn, None, dm, nthreads=thr)
-            O.inbatch_pullback(dSn, None, Qn, Dn, None, a, 1, dtype_code=2)
+        cpu_step, _, _ = c3_cpu_step(O, Q, D, dmask, dS, nsq, thr)
         dt, reps = time_cpu(cpu_step, min_seconds=5.0)
         full = dt * BQ3 / nsq
         v = 1.0 / full
         line = base_line(args, world, "in-batch fwd+bwd steps/sec", v, "steps/s", full * 1e3,
-                         "f32", cfg)
+                         "f32", cfg, scaling="weak")
         line.update(impl="reference",
                     cpu_baseline={"value": v, "unit": "steps/s", "cores": thr, "kind": "port",
-                                  "sample": f"{nsq} of 256 queries x all 256 docs (fwd + InvGrid "
+                                  "sample": f"{nsq} of 256 queries x all {bd} docs (fwd + InvGrid "
                                             f"bwd), {reps} repetitions, scaled x{BQ3 // nsq}"},
                     e2e={"value": v, "unit": "steps/s", "h2d_bytes_per_step": 0,
                          "d2h_bytes_per_step": 0})
@@ -317,8 +395,10 @@ def run_c3(args, world, rank, local, dev, fms):
     te, _ = tm.run(e2e_step, args.steps)
     te = max_over_ranks(te, world, dev)
     pk = peaks()
+    fwd_tape_ms = parts.get("fwd", 0) / args.steps
     fwd_ms = ms_f / args.steps
-    achieved = fwd_flop / (fwd_ms / 1e3) / 1e12
+    achieved = fwd_flop / (fwd_tape_ms / 1e3) / 1e12
+    step_tflops = (fwd_flop + bwd_flop) / (ms_step / 1e3) / 1e12
     line = base_line(args, world, "in-batch fwd+bwd steps/sec", value, "steps/s", ms_step, "bf16",
                      cfg, scaling="weak")
     line["e2e"] = {"value": world * args.steps / (te / 1e3), "unit": "steps/s",
@@ -328,28 +408,41 @@ def run_c3(args, world, rank, local, dev, fms):
     line["roofline"] = {"bound": "tensor", "achieved": achieved, "peak": pk["bf16"],
                         "unit": "TFLOP/s", "frac": achieved / pk["bf16"], "traffic": None,
                         "peak_source": f"{pk['src']} bf16_tflops (burst; the kernel is timed alone)",
-                        "kernel": "in-batch forward scan (scores-only launch)",
+                        "kernel": "in-batch forward scan with the argmax tape (the launch the "
+                                  "training step runs)",
                         "algorithmic_flop_per_launch": fwd_flop,
-                        "fwd_ms_with_tape": parts.get("fwd", 0) / args.steps,
-                        "fwd_ms_scores_only": fwd_ms,
-                        "bwd_ms": parts.get("bwd", 0) / args.steps}
+                        "fwd_ms_with_tape": fwd_tape_ms,
+                        "bwd_ms": parts.get("bwd", 0) / args.steps,
+                        "step": {"flop": fwd_flop + bwd_flop, "ms": ms_step,
+                                 "achieved_tflops": step_tflops,
+                                 "frac": step_tflops / pk["bf16"]},
+                        "scores_only_forward": {"ms": fwd_ms,
+                                                "frac": fwd_flop / (fwd_ms / 1e3) / 1e12 / pk["bf16"]}}
     line["clocks"] = clk
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0:
         O = oracle()
         nsq = 8
-        Qn, Dn = Q[:nsq].float().cpu().numpy(), D.float().cpu().numpy()
-        dm, dSn = dmask.cpu().numpy(), dS[:nsq].cpu().numpy()
         thr = O.default_threads()
-
-        def cpu_step():
-            S, a = O.inbatch(Qn, Dn, None, dm, nthreads=thr)
-            O.inbatch_pullback(dSn, None, Qn, Dn, None, a, 1, dtype_code=2)
-        dt, reps = time_cpu(cpu_step, min_seconds=5.0)
-        line["cpu_baseline"] = {"value": nsq / BQ3 / dt, "unit": "steps/s", "cores": thr,
-                                "kind": "port",
-                                "sample": f"{nsq} of 256 queries x all 256 docs (fwd + InvGrid "
-                                          f"bwd, f32 on bf16-rounded inputs), {reps} repetitions, "
-                                          f"scaled to 256 queries"}
+        cpu_step, Qn, Dn = c3_cpu_step(O, Q, D, dmask, dS, nsq, thr)
+        if not args.no_cpu_baseline:
+            dt, reps = time_cpu(cpu_step, min_seconds=5.0)
+            line["cpu_baseline"] = {"value": nsq / BQ3 / dt, "unit": "steps/s", "cores": thr,
+                                    "kind": "port",
+                                    "sample": f"{nsq} of 256 queries x all 256 docs (fwd + InvGrid "
+                                              f"bwd, f32 on bf16-rounded inputs), {reps} "
+                                              f"repetitions, scaled to 256 queries"}
+        So, Ao, dQo = cpu_step()
+        S, a = fms.inbatch_forward(Q, D, None, dmask, want_args=True)
+        dQ, _ = fms.inbatch_pullback(dS, Q, D, None, a, inv, fms.InvGrid())
+        ties, bad = args_check(a[:nsq].cpu().numpy(), Ao,
+                               lambda i, u: float(Qn[i[0], i[2]].astype(np.float64) @
+                                                  Dn[i[1], u - 1].astype(np.float64)), 1e-3)
+        line["parity"] = parity_record(
+            f"first {nsq} of 256 queries x all 256 documents: scores, argmax tape and dQ of a "
+            f"step run after the timed ones", max_rel_err(S[:nsq].cpu().numpy(), So), 1e-3, ties,
+            bad, checked=int(Ao.size),
+            dQ_max_rel_err=max_rel_err(dQ[:nsq].float().cpu().numpy(), dQo),
+            dQ_ok=max_rel_err(dQ[:nsq].float().cpu().numpy(), dQo) <= 1e-2)
     if rank == 0:
         print(json.dumps(line))
 
@@ -522,6 +615,25 @@ def run_c4(args, world, rank, local, dev, fms):
                         "tensor_frac": flop / (kms_step / 1e3) / 1e12 / pk["bf16"],
                         "kernel_ms": kms_step}
     line["clocks"] = clk
+    if rank == 0:
+        O = oracle()
+        nb = 200
+        cu = P.cu[:nb + 1].cpu().numpy()
+        ntb = int(cu[-1]) - 1
+        toks = P.tokens[:ntb].float().cpu().numpy()
+        Qn = Qs.float().cpu().numpy()
+        So, Ao = O.packed(Qn, toks, cu, nthreads=O.default_threads())
+        S = scan()
+        sub = fms.make_packed(P.tokens[:ntb], P.cu[:nb + 1])
+        _, A = fms.packed_forward(Qs, sub, want_args=True)
+        ties, bad = args_check(A.cpu().numpy(), Ao,
+                               lambda i, u: float(Qn[i[0], i[2]].astype(np.float64) @
+                                                  toks[cu[i[1]] - 2 + u].astype(np.float64)),
+                               1e-3)
+        line["parity"] = parity_record(
+            f"all 16 queries x the first {nb} documents of this GPU's packed gallery: scores of "
+            f"the scan launch the step runs, argmax tape of the same documents",
+            max_rel_err(S[:, :nb].cpu().numpy(), So), 1e-3, ties, bad, checked=int(Ao.size))
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         O = oracle()
         thr = O.default_threads()
@@ -651,11 +763,40 @@ def run_c5(args, world, rank, local, dev, fms):
                         "unit": "TOP/s", "frac": achieved / int8_peak, "traffic": None,
                         "peak_source": f"2 x {pk['src']} bf16_tflops (B200 dense int8 rate is "
                                        "twice bf16; no measured int8 peak)",
+                        "peak_assumed": True,
                         "kernel": "INT8 exhaustive scan (tcgen05 kind::i8), scores only",
                         "algorithmic_ops_per_launch": ops, "algorithmic_bytes_per_launch": byts,
                         "hbm_frac": byts / (scan_ms / 1e3) / 1e9 / pk["hbm"],
                         "scan_ms": scan_ms, "scan_plus_topk_ms": kms_step}
     line["clocks"] = clk
+    if rank == 0:
+        O = oracle()
+        thr = O.default_threads()
+        nb = 4000
+        vals, ids = fms.int8_exhaustive_forward(Q, index, topk=K5, id_offset=shard_lo - 1)
+        S = fms.int8_exhaustive_forward(None, index, quantized=qq)
+        Qc, Qsc = qq.codes.cpu().numpy(), qq.scales.float().cpu().numpy()
+        So = O.int8_exhaustive(Qc, Qsc, index.codes[:nb].cpu().numpy(),
+                               index.scales[:nb].cpu().numpy(), nthreads=thr)
+        # the top-k pass against a stable descending sort of the scan's scores
+        # (ties keep ascending ids)
+        order = torch.sort(S, dim=1, descending=True, stable=True).indices[:, :K5]
+        topk_ok = bool(torch.equal(ids, (order + shard_lo).to(torch.int32)))
+        # oracle scores of the returned documents of 4 queries
+        nsq = 4
+        pick = ids[:nsq].long() - shard_lo
+        err_top = 0.0
+        for r in range(nsq):
+            sub = pick[r]
+            Sr = O.int8_exhaustive(Qc[r:r + 1], Qsc[r:r + 1], index.codes[sub].cpu().numpy(),
+                                   index.scales[sub].cpu().numpy(), nthreads=thr)
+            err_top = max(err_top, max_rel_err(vals[r].cpu().numpy(), Sr[0]))
+        line["parity"] = parity_record(
+            f"scan scores of all 32 queries x the first {nb} documents vs the oracle; the "
+            f"top-{K5} ids vs a stable sort of the scan's scores (all queries); oracle scores of "
+            f"the returned documents of {nsq} queries", max_rel_err(S[:, :nb].cpu().numpy(), So),
+            1e-5, topk_ids_ok=topk_ok, topk_vals_max_rel_err=err_top,
+            topk_vals_ok=err_top <= 1e-5)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         O = oracle()
         thr = O.default_threads()

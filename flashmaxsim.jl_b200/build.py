@@ -3,6 +3,8 @@
 The library is the product: every MaxSim kernel plus the C ABI of
 include/fms.h.  It links the CUDA runtime dynamically (so it shares torch's /
 CUDA.jl's runtime state, e.g. the current device) and needs no other library.
+Each source compiles to its own object (in parallel, under _build/), then one
+link step makes the shared library.
 """
 from __future__ import annotations
 
@@ -10,6 +12,7 @@ import os
 import shutil
 import subprocess
 import sys
+from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
 
 PKG = Path(__file__).resolve().parent
@@ -17,6 +20,9 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 INCLUDE = ROOT / "include"
 LIB = PKG / "libflashmaxsim_sm100.so"
+OBJ = PKG / "_build"
+
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
 def nvcc() -> str:
@@ -41,23 +47,27 @@ def up_to_date() -> bool:
     return all(p.stat().st_mtime <= t for p in sources() + headers() + [Path(__file__)])
 
 
+def _compile(src: Path, verbose: bool) -> Path:
+    obj = OBJ / (src.stem + ".o")
+    cmd = [nvcc()] + ARCH + [
+        "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O3",
+        "-I", str(INCLUDE), "-I", str(CSRC), "-c", str(src), "-o", str(obj)]
+    if verbose:
+        cmd.insert(1, "-Xptxas=-v")
+    subprocess.check_call(cmd)
+    return obj
+
+
 def build(force: bool = False, verbose: bool = False) -> Path:
     if not force and up_to_date():
         return LIB
+    OBJ.mkdir(exist_ok=True)
+    with ThreadPoolExecutor(max_workers=max(1, min(len(sources()), os.cpu_count() or 1))) as ex:
+        objs = list(ex.map(lambda s: _compile(s, verbose), sources()))
     tmp = LIB.with_suffix(".so.tmp")
-    cmd = [
-        nvcc(),
-        "-gencode", "arch=compute_100a,code=sm_100a",
-        "-O3", "-lineinfo", "-std=c++17",
-        "-Xcompiler", "-fPIC,-O3",
-        "-shared", "-cudart", "shared",
-        "-Xlinker", "-rpath,/usr/local/cuda/lib64",
-        "-I", str(INCLUDE), "-I", str(CSRC),
-        "-o", str(tmp),
-    ] + [str(s) for s in sources()]
-    if verbose:
-        cmd.insert(1, "-Xptxas=-v")
-        print(" ".join(cmd))
+    cmd = [nvcc()] + ARCH + ["-shared", "-cudart", "shared",
+                             "-Xlinker", "-rpath,/usr/local/cuda/lib64", "-o", str(tmp)] + \
+        [str(o) for o in objs]
     subprocess.check_call(cmd)
     os.replace(tmp, LIB)
     return LIB

@@ -279,22 +279,56 @@ int fms_paired_bwd(int dtype, int strategy, const void* Delta, const void* inv_n
 // document tokens for Tq = 32 sources per 180-token document.
 static __device__ __align__(256) unsigned char g_static_scratch[FMS_STATIC_SCRATCH_BYTES];
 
+// The device address is cached per device together with the unique id of the
+// context it was looked up in: a primary context that was torn down and created
+// again (cudaDeviceReset, cuDevicePrimaryCtxReset) gets a new id, the module --
+// and with it the array -- is loaded again, and the set-up runs again.
 static void* g_scratch_addr[64];
+static unsigned long long g_scratch_ctx[64];
 static std::mutex g_scratch_mu;
 
-// Device address of the scratch on the current device, looked up once per
-// device (cudaGetSymbolAddress) and cached.
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long*);
+
+// Unique id of the calling thread's current context, 0 when there is none yet
+// (or the driver does not offer the query: the address is then looked up anew).
+static unsigned long long current_ctx_id() {
+  static CtxGetCurrentFn get_cur = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_cur = reinterpret_cast<CtxGetCurrentFn>(p);
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(p);
+  });
+  if (!get_cur || !get_id) return 0;
+  CUcontext c = nullptr;
+  unsigned long long id = 0;
+  if (get_cur(&c) != CUDA_SUCCESS || c == nullptr || get_id(c, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
+
+// Set-up of the scratch on the current device: its device address
+// (cudaGetSymbolAddress, return code checked), looked up once per device and
+// context and cached.
 static cudaError_t static_scratch(void** out) {
   int d = 0;
   cudaError_t e = cudaGetDevice(&d);
   if (e != cudaSuccess) return e;
   if (d < 0 || d >= 64) return cudaErrorInvalidDevice;
   std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (g_scratch_addr[d] == nullptr) {
+  const unsigned long long ctx = current_ctx_id();
+  if (g_scratch_addr[d] == nullptr || ctx == 0 || ctx != g_scratch_ctx[d]) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_static_scratch);
     if (e != cudaSuccess) return e;
     g_scratch_addr[d] = p;
+    g_scratch_ctx[d] = current_ctx_id();  // the lookup above made the context current
   }
   *out = g_scratch_addr[d];
   return cudaSuccess;

@@ -13,8 +13,10 @@
 //    replacing the reference's one-thread serial prefix -> atomic fill), then a
 //    destination-owned scatter: a warp per document token sums its sources in
 //    ascending source order (segments up to 1024 sources are ranked in shared
-//    memory), so dD is deterministic run to run, unlike the reference's
-//    atomic-order fill.  The dQ gather is the same warp-per-token kernel.
+//    memory by the scatter warp; longer segments are sorted in place first, one
+//    block each), so dD is deterministic run to run whatever the segment
+//    lengths, unlike the reference's atomic-order fill.  The dQ gather is the
+//    same warp-per-token kernel.
 // Accumulation is float32 (float64 for T = Float64) and each gradient element
 // is rounded to T once.
 #include "fms_common.cuh"
@@ -136,14 +138,19 @@ __global__ void csr_count_kernel(ScanParams p, int64_t n_src, int32_t* __restric
 }
 
 constexpr int SCAN_BLOCK = 1024;
+constexpr int SC_SEG = 1024;  // sources ranked per destination in shared memory
 
 // In-place exclusive scan, phase 1: each block scans 1024 entries and records
-// its total.
+// its total.  Destinations with more than SC_SEG sources (counts x[i]) are
+// appended to long_list (long_cnt counts them) for the segment sort.
 __global__ void __launch_bounds__(SCAN_BLOCK) scan_blocks_kernel(int32_t* __restrict__ x, int64_t n,
-                                                                int32_t* __restrict__ block_sums) {
+                                                                int32_t* __restrict__ block_sums,
+                                                                int32_t* __restrict__ long_cnt,
+                                                                int32_t* __restrict__ long_list) {
   __shared__ int32_t warp_sums[32];
   int64_t i = (int64_t)blockIdx.x * SCAN_BLOCK + threadIdx.x;
   int32_t v = (i < n) ? x[i] : 0;
+  if (v > SC_SEG) long_list[atomicAdd(long_cnt, 1)] = (int32_t)i;
   int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   int32_t incl = v;
 #pragma unroll
@@ -228,8 +235,88 @@ __global__ void csr_fill_kernel(ScanParams p, int64_t n_src, int32_t* __restrict
   }
 }
 
+// Segments longer than SC_SEG: sorted ascending in place, one block per segment
+// (block-stride over the list of long segments).  Tiles of SORT_TILE ids are
+// bitonic-sorted in shared memory, then sorted runs are merged pairwise: the
+// ids of a segment are distinct, so an id's place in the merged run is its
+// index in its own run plus the number of smaller ids in the sibling run (a
+// binary search).  Runs ping-pong between the segment and the same offsets of
+// `tmp`, and end in the segment.
+constexpr int SORT_TILE = 2048;
+constexpr int SORT_THREADS = 1024;
+
+__device__ __forceinline__ int lower_bound_i32(const int32_t* a, int n, int32_t x) {
+  int lo = 0, hi = n;
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (a[mid] < x) lo = mid + 1; else hi = mid;
+  }
+  return lo;
+}
+
+__global__ void __launch_bounds__(SORT_THREADS) csr_sort_long_kernel(const int32_t* __restrict__ row_ptr,
+                                                                     int32_t* __restrict__ col_idx,
+                                                                     int32_t* __restrict__ tmp,
+                                                                     const int32_t* __restrict__ long_cnt,
+                                                                     const int32_t* __restrict__ long_list) {
+  __shared__ int32_t tile[SORT_TILE];
+  const int nlong = *long_cnt;
+  for (int li = blockIdx.x; li < nlong; li += gridDim.x) {
+    const int32_t d = long_list[li];
+    const int32_t a0 = row_ptr[d];
+    const int n = row_ptr[d + 1] - a0;
+    int32_t* seg = col_idx + a0;
+    int32_t* alt = tmp + a0;
+    // sorted tiles
+    for (int t0 = 0; t0 < n; t0 += SORT_TILE) {
+      const int len = min(SORT_TILE, n - t0);
+      __syncthreads();
+      for (int i = threadIdx.x; i < SORT_TILE; i += SORT_THREADS) tile[i] = i < len ? seg[t0 + i] : INT32_MAX;
+      for (int size = 2; size <= SORT_TILE; size <<= 1) {
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+          __syncthreads();
+          for (int i = threadIdx.x; i < SORT_TILE / 2; i += SORT_THREADS) {
+            const int lo = 2 * i - (i & (stride - 1));
+            const int hi = lo + stride;
+            const bool asc = (lo & size) == 0;
+            const int32_t x = tile[lo], y = tile[hi];
+            if ((x > y) == asc) { tile[lo] = y; tile[hi] = x; }
+          }
+        }
+      }
+      __syncthreads();
+      for (int i = threadIdx.x; i < len; i += SORT_THREADS) seg[t0 + i] = tile[i];
+    }
+    // pairwise merges of sorted runs of width w
+    const int32_t* src = seg;
+    int32_t* dst = alt;
+    for (int w = SORT_TILE; w < n; w <<= 1) {
+      __syncthreads();
+      for (int p = threadIdx.x; p < n; p += SORT_THREADS) {
+        const int r = p / w;
+        const int base = (r & ~1) * w;
+        const int32_t x = src[p];
+        int pos;
+        if ((r & 1) == 0) {
+          const int lenb = min(w, max(0, n - (base + w)));
+          pos = p + lower_bound_i32(src + base + w, lenb, x);
+        } else {
+          pos = base + (p - (base + w)) + lower_bound_i32(src + base, w, x);
+        }
+        dst[pos] = x;
+      }
+      const int32_t* t = src;
+      src = dst;
+      dst = const_cast<int32_t*>(t);
+    }
+    __syncthreads();
+    if (src != seg)
+      for (int p = threadIdx.x; p < n; p += SORT_THREADS) seg[p] = src[p];
+    __syncthreads();
+  }
+}
+
 constexpr int SC_WARPS = 8;
-constexpr int SC_SEG = 1024;  // sources ranked per destination in shared memory
 
 // Warp per destination document token; sources summed in ascending id order.
 template <typename T>
@@ -592,10 +679,14 @@ size_t bwd_workspace_bytes(int strategy, int dtype, int64_t n_src, int64_t n_des
     if (dtype == FMS_F16 || dtype == FMS_BF16) return align_up((size_t)grad_d_numel * 4, 256);
     return 0;
   }
+  // row_ptr (+ the long-segment count), cursor, col_idx, scan partials, the
+  // list of long segments and the segment sort's ping-pong buffer
   size_t nscan = (size_t)n_dest + 1;
   size_t nb = (nscan + SCAN_BLOCK - 1) / SCAN_BLOCK;
-  return align_up(nscan * 4, 256) + align_up((size_t)n_dest * 4 + 4, 256) +
-         align_up((size_t)n_src * 4 + 4, 256) + align_up(nb * 4 + 4, 256);
+  size_t nlong = (size_t)n_src / (SC_SEG + 1) + 1;
+  return align_up(nscan * 4 + 4, 256) + align_up((size_t)n_dest * 4 + 4, 256) +
+         align_up((size_t)n_src * 4 + 4, 256) + align_up(nb * 4 + 4, 256) +
+         align_up(nlong * 4, 256) + align_up((size_t)n_src * 4 + 4, 256);
 }
 
 template <typename T>
@@ -640,14 +731,20 @@ static cudaError_t run_backward(int strategy, const BwdParams& b, void* ws, size
   if (ws == nullptr || ws_bytes < need) return cudaErrorInvalidValue;
   const int64_t nscan = n_dest + 1;
   const int64_t nb = (nscan + SCAN_BLOCK - 1) / SCAN_BLOCK;
+  const size_t nlong = (size_t)n_src / (SC_SEG + 1) + 1;
   char* w = static_cast<char*>(ws);
   int32_t* row_ptr = reinterpret_cast<int32_t*>(w);
-  w += align_up((size_t)nscan * 4, 256);
+  int32_t* long_cnt = row_ptr + nscan;  // cleared with row_ptr
+  w += align_up((size_t)nscan * 4 + 4, 256);
   int32_t* cursor = reinterpret_cast<int32_t*>(w);
   w += align_up((size_t)n_dest * 4 + 4, 256);
   int32_t* col_idx = reinterpret_cast<int32_t*>(w);
   w += align_up((size_t)n_src * 4 + 4, 256);
   int32_t* sums = reinterpret_cast<int32_t*>(w);
+  w += align_up((size_t)nb * 4 + 4, 256);
+  int32_t* long_list = reinterpret_cast<int32_t*>(w);
+  w += align_up(nlong * 4, 256);
+  int32_t* sort_tmp = reinterpret_cast<int32_t*>(w);
 
   // dQ gather (no atomics)
   if (!launch_gather_vec<T, false>(b, nullptr, grid_for(b.nq_rows, 8), s))
@@ -655,12 +752,12 @@ static cudaError_t run_backward(int strategy, const BwdParams& b, void* ws, size
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   // counting sort: counts land at row_ptr[dest], exclusive scan turns them into
   // segment starts, row_ptr[n_dest] = nnz.
-  if ((e = cudaMemsetAsync(row_ptr, 0, (size_t)nscan * 4, s)) != cudaSuccess) return e;
+  if ((e = cudaMemsetAsync(row_ptr, 0, (size_t)nscan * 4 + 4, s)) != cudaSuccess) return e;
   if (n_src > 0) {
     csr_count_kernel<<<grid_for(n_src, 256), 256, 0, s>>>(p, n_src, row_ptr);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
-  scan_blocks_kernel<<<(unsigned)nb, SCAN_BLOCK, 0, s>>>(row_ptr, nscan, sums);
+  scan_blocks_kernel<<<(unsigned)nb, SCAN_BLOCK, 0, s>>>(row_ptr, nscan, sums, long_cnt, long_list);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   scan_sums_kernel<<<1, SCAN_BLOCK, 0, s>>>(sums, nb);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
@@ -669,6 +766,13 @@ static cudaError_t run_backward(int strategy, const BwdParams& b, void* ws, size
   if (n_src > 0) {
     csr_fill_kernel<<<grid_for(n_src, 256), 256, 0, s>>>(p, n_src, cursor, col_idx);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    // segments over SC_SEG sources: ascending order before the scatter (a
+    // no-op launch when there are none)
+    if (n_src > SC_SEG) {
+      csr_sort_long_kernel<<<(unsigned)sms, SORT_THREADS, 0, s>>>(row_ptr, col_idx, sort_tmp, long_cnt,
+                                                                  long_list);
+      if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    }
   }
   if (n_dest > 0) {
     if (!launch_scatter_vec<T>(b, row_ptr, col_idx, grid_for(n_dest, SC_WARPS), s))

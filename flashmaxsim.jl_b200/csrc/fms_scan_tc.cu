@@ -231,8 +231,10 @@ __device__ __forceinline__ void load_doc_rows(unsigned char* sB, const BMaps& bm
   if (nr - r >= 16) { ptx::tma_load_2d(sB + r * ROWB, &bm.b16, x, (int)(row + r), bar); r += 16; }
 }
 
+// Every configuration runs two CTAs per SM (launch_cfg), so registers are
+// capped for two co-resident 224-thread CTAs.
 template <int M, int NT, int MAXMT, int R, int NACC, int SMAX, int ARES, bool ARGS>
-__global__ void __launch_bounds__(NTHREADS, 1)
+__global__ void __launch_bounds__(NTHREADS, 2)
 tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ BMaps bm, TcParams P,
                int S) {
   using L = Cfg<M, NT, MAXMT, R, NACC, SMAX, ARES>;

@@ -71,21 +71,33 @@ def finalize_neg(idxs, n_global, neg, S):
     return S
 
 
-def merge_candidate_scores(S_local, idxs, n_global, neg, finalize=finalize_neg, group=None):
-    """All-reduce(max) of owner-disjoint shard scores, then the `neg` fill."""
+def _no_mark(name):
+    pass
+
+
+def merge_candidate_scores(S_local, idxs, n_global, neg, finalize=finalize_neg, group=None,
+                           mark=None):
+    """All-reduce(max) of owner-disjoint shard scores, then the `neg` fill.
+    `mark(name)` (optional) is called after each phase, e.g. to record events."""
+    mark = mark or _no_mark
     if dist.is_initialized() and dist.get_world_size(group) > 1:
         dist.all_reduce(S_local, op=dist.ReduceOp.MAX, group=group)
-    return finalize(idxs, n_global, neg, S_local)
+    mark("allreduce")
+    S = finalize(idxs, n_global, neg, S_local)
+    mark("finalize")
+    return S
 
 
 def sharded_candidates(Q, gallery_shard, idxs, qmask, dmask_shard, shard_lo, n_global,
-                       neg=-1.0e4, normalize=False, group=None):
+                       neg=-1.0e4, normalize=False, group=None, mark=None):
     """maxsim(Q, gallery, idxs, ...) with the gallery sharded over the group.
     Returns the full (B, C) scores on every rank."""
     S = candidates_shard_forward(Q, gallery_shard, idxs, qmask, dmask_shard, shard_lo,
                                  normalize)
+    if mark:
+        mark("scan")
     negv = L._neg_value(neg, Q.dtype)
-    return merge_candidate_scores(S, idxs, n_global, negv, group=group)
+    return merge_candidate_scores(S, idxs, n_global, negv, group=group, mark=mark)
 
 
 def merge_topk(vals, ids, k, merge=None, group=None):

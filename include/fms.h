@@ -4,7 +4,7 @@
  * This is the drop-in boundary for FlashMaxSim.jl's CUDA path.  Each entry point
  * replaces one layout driver of the reference (file:line in FlashMaxSim.jl
  * v0.1.2 given beside it); the Julia package binds them with `ccall` from a
- * package extension (see INTEGRATION.md), Python binds them with ctypes.
+ * package extension, Python binds them with ctypes.
  *
  * Conventions (the reference's own, so Julia arrays pass straight through):
  *  - All arrays are device pointers, contiguous and column-major with tokens as
@@ -167,9 +167,11 @@ int fms_paired_bwd(int dtype, int strategy, const void* Delta, const void* inv_n
    FMS_STATIC_SCRATCH_BYTES inside this library; the call allocates nothing.
    - Inputs whose InvGrid scratch (fms_bwd_workspace_size(FMS_INVGRID, ...))
      exceeds FMS_STATIC_SCRATCH_BYTES return FMS_ERR_TOO_LARGE before any work.
-   - The scratch address is looked up once per device (cudaGetSymbolAddress) on
-     the first call on that device; make that first call before any stream
-     capture begins.
+   - The scratch address is looked up (cudaGetSymbolAddress) on the first call
+     on a device and again on the first call after that device's primary context
+     was torn down and created anew (cudaDeviceReset reloads the library's
+     device code, so the array may move); make that first call before any
+     stream capture begins.
    - One scratch per device: calls that overlap in time on the same device (other
      streams, other host threads) race on it and corrupt each other's results.
      Serialise them.

@@ -140,7 +140,14 @@ def _fn(name, acc):
 
 
 def default_threads() -> int:
-    return lib().fmso_num_threads()
+    """Host cores this process may run on (not omp_get_max_threads(): launchers
+    such as torchrun set OMP_NUM_THREADS=1, and every oracle entry point takes
+    its thread count explicitly)."""
+    import os
+    try:
+        return max(1, len(os.sched_getaffinity(0)))
+    except (AttributeError, OSError):
+        return max(1, os.cpu_count() or 1)
 
 
 # --------------------------------------------------------------------------- forward

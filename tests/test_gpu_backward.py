@@ -170,3 +170,56 @@ def test_inbatch_pullback_wide_rows(fms, oracle, code, name, dim):
     if code == 1:
         dQ2, dD2 = fms.inbatch_pullback(Delta, Q, D, None, args, None, strategy(fms, code))
         assert torch.equal(dD, dD2) and torch.equal(dQ, dQ2)
+
+
+def _hub_queries(rng, n, Tq, dim, v, dtype):
+    """Query tokens close to the direction v (each one's best match is v)."""
+    x = v[None, None, :] + 0.1 * rng.standard_normal((n, Tq, dim))
+    return torch.from_numpy(l2cols(x)).to(dtype).cuda()
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_invgrid_long_segments_deterministic(fms, oracle, dtype):
+    """Destinations that are the argmax of more than 1024 sources (hub tokens)
+    still sum their sources in ascending source order: two runs are bit for
+    bit identical and match the oracle's ascending-order CSR sum.  In-batch:
+    40 queries x 32 tokens = 1280 sources on one token of each of two docs;
+    candidates: 51,200 sources on one gallery token (several merge passes of
+    the segment sort)."""
+    rng = seeded(48)
+    dim = 64
+    v = l2cols(rng.standard_normal(dim))
+    Bq, Tq, Bd, Td = 40, 32, 5, 30
+    Q = _hub_queries(rng, Bq, Tq, dim, v, dtype)
+    Dn = l2cols(rng.standard_normal((Bd, Td, dim)))
+    Dn[0, 3] = v
+    Dn[1, 0] = v
+    D = torch.from_numpy(Dn).to(dtype).cuda()
+    _, args = fms.inbatch_forward(Q, D)
+    assert (args[:, 0, :] == 4).all() and (args[:, 1, :] == 1).all()
+    Delta = torch.randn(Bq, Bd, device="cuda")
+    runs = [fms.inbatch_pullback(Delta, Q, D, None, args, None, fms.InvGrid()) for _ in range(2)]
+    assert torch.equal(runs[0][1], runs[1][1]) and torch.equal(runs[0][0], runs[1][0])
+    dcode = 0 if dtype == torch.float32 else 2
+    dQo, dDo = oracle.inbatch_pullback(Delta.to(dtype), None, Q, D, None, args.cpu(), 1, dcode)
+    tol = 1e-5 if dtype == torch.float32 else 1e-2
+    close(runs[0][0], dQo, tol, "dQ")
+    close(runs[0][1], dDo, tol, "dD")
+
+    B, C, N = 4, 400, 9
+    Qc = _hub_queries(rng, B, Tq, dim, v, dtype)
+    Gn = l2cols(rng.standard_normal((N, Td, dim)))
+    Gn[5, 7] = v
+    G = torch.from_numpy(Gn).to(dtype).cuda()
+    idxs = torch.full((B, C), 6, dtype=torch.int32, device="cuda")
+    idxs[:, ::7] = torch.from_numpy(rng.integers(1, N + 1, (B, len(range(0, C, 7))))
+                                   .astype(np.int32)).cuda()
+    _, cargs = fms.candidates_forward(Qc, G, idxs)
+    Dl = torch.randn(B, C, device="cuda")
+    r1 = fms.candidates_pullback(Dl, Qc, G, idxs, None, cargs, None, fms.InvGrid())
+    r2 = fms.candidates_pullback(Dl, Qc, G, idxs, None, cargs, None, fms.InvGrid())
+    assert torch.equal(r1[1], r2[1]) and torch.equal(r1[0], r2[0])
+    dQo, dGo = oracle.candidates_pullback(Dl.to(dtype), None, Qc, G, idxs.cpu(), None, cargs.cpu(),
+                                          1, dcode)
+    close(r1[0], dQo, tol, "cand dQ")
+    close(r1[1], dGo, tol, "cand dG")

@@ -144,7 +144,12 @@ def test_varlen(fms, oracle, dt):
         S, A = fms.varlen_forward(Qp, Dp, normalize=norm)
         So, Ao = oracle.varlen(Qp.tokens, Dp.tokens, Qp.cu.cpu(), Dp.cu.cpu(), normalize=norm)
         assert_scores(S.cpu(), So, tol)
-        assert (A.cpu().numpy() == Ao).mean() > 0.99
+        qt, dt = Qp.tokens.cpu(), Dp.tokens.cpu()
+        cq, cd = Qp.cu.cpu().numpy(), Dp.cu.cpu().numpy()
+        assert_args(A.cpu(), Ao,
+                    lambda i, u: sim_pair(qt[cq[i[0]] - 1 + i[1]:cq[i[0]] + i[1]],
+                                          dt[cd[i[0]] - 1 + u - 1:cd[i[0]] - 1 + u])[0, 0],
+                    tie)
 
 
 def test_edge_shapes(fms):
@@ -183,7 +188,8 @@ def test_golden_fixtures(fms):
     dm = torch.from_numpy(g["dmask"]).cuda()
     s, a = fms.paired_forward(Q, D, qm, dm)
     assert_scores(s.cpu(), g["paired_scores"], 1e-5)
-    assert (a.cpu().numpy() == g["paired_args"]).mean() > 0.99
+    assert_args(a.cpu(), g["paired_args"],
+                lambda i, u: sim_pair(Q[i[0]].cpu(), D[i[0]].cpu())[i[1], u - 1], 1e-4)
     S, A = fms.inbatch_forward(Q, D, qm, dm)
     assert_scores(S.cpu(), g["inbatch_S"], 1e-5)
     G = torch.from_numpy(g["G"]).cuda()
