@@ -358,11 +358,19 @@ def main():
     ntok, nslots = doc_tokens(idxs, lens, world, rank)
     neg = float("-inf")
     lo = rank * NDOC + 1
+    # N > 1: the library's NCCL entry point (scan of the owned slots, all-reduce,
+    # `neg` fill in one call on this stream), over a communicator of the group
+    comm = fdist.Comm.from_group(device=dev) if world > 1 else None
 
     def step(mark=None):
         if world == 1:
             return fms.candidates_forward(Q, gallery, idxs, None, dmask, neg=neg,
                                           want_args=False)[0]
+        if mark is None:
+            return fdist.sharded_candidates_abi(comm, Q, gallery, idxs, None, dmask, lo,
+                                                NDOC * world, neg=neg)
+        # the same kernels with the exchange through torch.distributed, so that
+        # events can separate the phases
         return fdist.sharded_candidates(Q, gallery, idxs, None, dmask, shard_lo=lo,
                                         n_global=NDOC * world, neg=neg, mark=mark)
 
@@ -397,8 +405,9 @@ def main():
     ms_step = ms_max / args.steps
     value = total_tok * args.steps / (ms_max / 1e3)
 
-    # per-phase device time of the sharded step (separate untimed pass with events
-    # between the phases), mean per step, max over ranks
+    # per-phase device time of the sharded step (a separate untimed pass of the
+    # same kernels with events between the phases and the exchange through
+    # torch.distributed's NCCL), mean per step, max over ranks
     phases = None
     if world > 1:
         acc = {}
@@ -430,8 +439,8 @@ def main():
         if world == 1:
             Sd = fms.maxsim(Qd, gallery, idd, None, dmask, neg=neg)
         else:
-            Sd = fdist.sharded_candidates(Qd, gallery, idd, None, dmask, shard_lo=lo,
-                                          n_global=NDOC * world, neg=neg)
+            Sd = fdist.sharded_candidates_abi(comm, Qd, gallery, idd, None, dmask, lo,
+                                              NDOC * world, neg=neg)
         Sh.copy_(Sd, non_blocking=True)
 
     for _ in range(2):
@@ -457,7 +466,7 @@ def main():
     alg_bytes = ntok * DIM * 2 + nslots * TD + Q.numel() * 2 + idxs.numel() * 4 + \
         idxs.numel() * 4
     peak, peak_kind = measured_peaks()
-    scan_ms = phases["scan"] if phases else ms_step
+    scan_ms = phases["scan"] if phases else ms_step  # the scan launch alone
     achieved = alg_bytes / (scan_ms / 1e3) / 1e9
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -468,6 +477,7 @@ def main():
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h,
                 "note": "gallery resident in HBM (index); queries+idxs H2D, scores D2H"},
+        # N=1: the scan; N>1: list compaction, scan, finalize (+ NCCL's all-reduce)
         "gpu_launches": args.steps * (1 if world == 1 else 3),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": None,
@@ -500,6 +510,7 @@ def main():
         print(json.dumps(line))
     if world > 1:
         dist.barrier()
+        comm.close()
         dist.destroy_process_group()
 
 

@@ -44,8 +44,9 @@ SIGNATURES = {
     "fms_inbatch_fwd": (_i, [_i, _P, _P, _P, _P, _i, _i, _i, _i, _i, _i, _P, _P, _P]),
     "fms_candidates_fwd": (_i, [_i, _P, _P, _P, _P, _P, _i, _i, _i, _i, _i64, _i, _d, _i, _P,
                                 _P, _P]),
+    "fms_candidates_shard_workspace_size": (_sz, [_i, _i]),
     "fms_candidates_shard_fwd": (_i, [_i, _P, _P, _P, _P, _P, _i, _i, _i, _i, _i64, _i, _i64,
-                                      _i, _P, _P]),
+                                      _i, _P, _P, _sz, _P]),
     "fms_packed_fwd": (_i, [_i, _P, _P, _P, _P, _i, _i, _i, _i, _i64, _i, _P, _P, _P]),
     "fms_varlen_fwd": (_i, [_i, _P, _P, _P, _P, _i, _i, _i, _i64, _i64, _i, _P, _P, _P]),
     "fms_inv_counts": (_i, [_i, _P, _i, _i, _P, _P]),
@@ -72,6 +73,23 @@ SIGNATURES = {
                                      _P, _i, _P, _P, _i64, _P, _sz, _P]),
     "fms_topk_merge": (_i, [_P, _P, _i, _i, _i, _P, _P, _P]),
     "fms_candidates_finalize_neg": (_i, [_P, _i64, _i, _i, _d, _P, _P]),
+    # multi-GPU (NCCL)
+    "fms_nccl_available": (_i, []),
+    "fms_last_nccl_error": (C.c_char_p, []),
+    "fms_comm_unique_id": (_i, [_P]),
+    "fms_comm_init": (_i, [_P, _i, _i, _P]),
+    "fms_comm_from_nccl": (_i, [_P, _P]),
+    "fms_comm_destroy": (_i, [_P]),
+    "fms_comm_size": (_i, [_P, _P, _P]),
+    "fms_sharded_candidates_workspace_size": (_sz, [_i, _i]),
+    "fms_sharded_candidates_fwd": (_i, [_P, _i, _P, _P, _P, _P, _P, _i, _i, _i, _i, _i64, _i,
+                                        _i64, _i64, _d, _i, _P, _P, _sz, _P]),
+    "fms_sharded_packed_workspace_size": (_sz, [_i, _i, _i]),
+    "fms_sharded_packed_fwd": (_i, [_P, _i, _P, _P, _P, _P, _i, _i, _i, _P, _i64, _i, _P, _P,
+                                    _sz, _P]),
+    "fms_sharded_int8_topk_workspace_size": (_sz, [_i, _i, _i64, _i]),
+    "fms_sharded_int8_topk": (_i, [_P, _i, _i, _P, _P, _P, _P, _P, _P, _i, _i, _i, _i, _i64,
+                                   _i64, _i, _i, _P, _P, _P, _sz, _P]),
 }
 
 
@@ -105,6 +123,8 @@ def lib():
 def check(status: int, what: str):
     if status != 0:
         msg = lib().fms_status_string(status).decode()
+        if status == -7:
+            msg += ": " + lib().fms_last_nccl_error().decode()
         if status == -1:
             from .errors import DimensionMismatch
             raise DimensionMismatch(f"{what}: {msg}")

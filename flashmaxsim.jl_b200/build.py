@@ -2,7 +2,9 @@
 
 The library is the product: every MaxSim kernel plus the C ABI of
 include/fms.h.  It links the CUDA runtime dynamically (so it shares torch's /
-CUDA.jl's runtime state, e.g. the current device) and needs no other library.
+CUDA.jl's runtime state, e.g. the current device) and needs no other library
+at link time (NCCL is opened at run time by the multi-GPU entry points; its
+header, nccl.h, is needed to build).
 Each source compiles to its own object (in parallel, under _build/), then one
 link step makes the shared library.
 """
@@ -67,7 +69,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     tmp = LIB.with_suffix(".so.tmp")
     cmd = [nvcc()] + ARCH + ["-shared", "-cudart", "shared",
                              "-Xlinker", "-rpath,/usr/local/cuda/lib64", "-o", str(tmp)] + \
-        [str(o) for o in objs]
+        [str(o) for o in objs] + ["-ldl"]
     subprocess.check_call(cmd)
     os.replace(tmp, LIB)
     return LIB

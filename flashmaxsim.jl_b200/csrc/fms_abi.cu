@@ -89,11 +89,12 @@ const char* fms_status_string(int status) {
     case FMS_ERR_WORKSPACE: return "workspace missing or too small";
     case FMS_ERR_UNSUPPORTED: return "unsupported device or feature";
     case FMS_ERR_TOO_LARGE: return "input too large for the fixed scratch of a no-allocation entry point";
+    case FMS_ERR_NCCL: return "an NCCL call failed (fms_last_nccl_error)";
     default: return status > 0 ? cudaGetErrorString((cudaError_t)status) : "unknown error";
   }
 }
 
-int fms_version(void) { return 100; }
+int fms_version(void) { return 10100; }
 
 int fms_device_error(int reset) {
   const int a = read_device_error(reset);
@@ -158,12 +159,20 @@ int fms_candidates_shard_fwd(int dtype, const void* Q, const void* gallery_shard
                              const int32_t* idxs, const uint8_t* qmask,
                              const uint8_t* dmask_shard, int dim, int Tq, int B, int Td,
                              int64_t N_local, int C, int64_t id_lo, int normalize, void* S,
-                             fms_stream_t stream) {
+                             void* workspace, size_t ws_bytes, fms_stream_t stream) {
   if (!dtype_ok(dtype)) return FMS_ERR_DTYPE;
   if (dim < 0 || Tq < 0 || B < 0 || Td < 0 || N_local < 0 || C < 0 || id_lo < 1)
     return FMS_ERR_INVALID;
   if ((int64_t)C * B > 0 && (!S || !idxs)) return FMS_ERR_INVALID;
+  if (workspace && ws_bytes < shard_list_bytes((int64_t)C * B)) return FMS_ERR_WORKSPACE;
+  if (workspace && dtype == FMS_F64) return FMS_ERR_DTYPE;  // the list path writes float32 -Inf
   ScanParams p = base_params();
+  if (workspace && (int64_t)C * B > 0) {
+    cudaError_t e = launch_shard_compact(idxs, (int64_t)C * B, id_lo, N_local, workspace,
+                                         static_cast<float*>(S), &p.unit_list, &p.unit_count,
+                                         (cudaStream_t)stream);
+    if (e != cudaSuccess) return (int)e;
+  }
   p.layout = L_CANDIDATES;
   p.Q = Q; p.D = gallery_shard; p.qmask = qmask; p.dmask = dmask_shard; p.idxs = idxs;
   p.dim = dim; p.Tq = Tq; p.Td = Td; p.B = B; p.C = C; p.Ngal = N_local;

@@ -47,7 +47,20 @@ struct ScanParams {
   double neg;
   void* scores;             // score_eltype(T)
   int32_t* args;            // NULL = scores only
+  // Optional device list of the unit ids to scan (a sharded candidate scan
+  // scans only the slots its shard owns) and its device-resident length; the
+  // scans then walk list entries 0 .. *unit_count - 1 instead of 0 .. nunits-1.
+  const int32_t* unit_list;
+  const int32_t* unit_count;
 };
+
+// Units a scan walks (device side) and the unit id of walk position v.
+__device__ __forceinline__ int64_t units_to_scan(const ScanParams& p) {
+  return p.unit_count ? (int64_t)*p.unit_count : p.nunits;
+}
+__device__ __forceinline__ int64_t unit_at(const ScanParams& p, int64_t v) {
+  return p.unit_list ? (int64_t)p.unit_list[v] : v;
+}
 
 // Backward geometry: the forward's ScanParams plus cotangents and outputs.
 struct BwdParams {

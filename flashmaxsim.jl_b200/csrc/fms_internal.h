@@ -34,4 +34,12 @@ size_t bwd_workspace_bytes(int strategy, int dtype, int64_t n_src, int64_t n_des
 cudaError_t launch_backward(int dtype, int strategy, const BwdParams& b, void* ws,
                             size_t ws_bytes, cudaStream_t s);
 
+// Sharded candidates: list the slots of idxs (nslots) whose doc is one of this
+// shard's n_local docs starting at id_lo into the workspace (shard_list_bytes),
+// writing -Inf into S for every other slot; *list / *count point into it.
+size_t shard_list_bytes(int64_t nslots);
+cudaError_t launch_shard_compact(const int32_t* idxs, int64_t nslots, int64_t id_lo, int64_t n_local,
+                                 void* ws, float* S, const int32_t** list, const int32_t** count,
+                                 cudaStream_t s);
+
 }  // namespace fms

@@ -40,7 +40,9 @@ simt_scan_kernel(ScanParams p) {
   const int dim = p.dim;
   A* scores = static_cast<A*>(p.scores);
 
-  for (int64_t unit = blockIdx.x; unit < p.nunits; unit += gridDim.x) {
+  const int64_t nwalk = units_to_scan(p);
+  for (int64_t v = blockIdx.x; v < nwalk; v += gridDim.x) {
+    const int64_t unit = unit_at(p, v);
     const Unit U = decode_unit(p, unit);
     if (!U.valid) {
       if (tid == 0) scores[U.out] = (A)p.neg;

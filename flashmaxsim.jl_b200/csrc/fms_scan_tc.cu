@@ -302,9 +302,11 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem_base = tmem_base_s;
-  // a contiguous range of units per CTA (query tiles change rarely along it)
-  const int64_t u_begin = P.nunits * blockIdx.x / gridDim.x;
-  const int64_t my_units = P.nunits * (blockIdx.x + 1) / gridDim.x - u_begin;
+  // a contiguous range of units (or of unit-list entries) per CTA (query tiles
+  // change rarely along it)
+  const int64_t nwalk = p.unit_count ? (int64_t)*p.unit_count : P.nunits;
+  const int64_t u_begin = nwalk * blockIdx.x / gridDim.x;
+  const int64_t my_units = nwalk * (blockIdx.x + 1) / gridDim.x - u_begin;
   // K blocks per ring stage and stages per chunk
   const int kbs = ARES ? P.KB : 1;
   const int spc = ARES ? 1 : P.KB;
@@ -321,7 +323,7 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       UnitMeta m;
       int working = 0, direct = 0;
       if (i < my_units) {
-        const TcUnit U = tc_decode(P, u_begin + i);
+        const TcUnit U = tc_decode(P, unit_at(p, u_begin + i));
         m.q_row0 = U.q_row0; m.d_row0 = U.d_row0;
         m.out0 = U.out0; m.out_stride = U.out_stride;
         m.arg0 = U.arg0; m.arg_stride = U.arg_stride;
@@ -907,8 +909,8 @@ cudaError_t launch_scan_tc(int dtype, const ScanParams& p, cudaStream_t s) {
       !tc::make_map(&bm.b32, p.D, P.fmt, p.dim, p.nd_tok, 32) ||
       !tc::make_map(&bm.b16, p.D, P.fmt, p.dim, p.nd_tok, 16))
     return cudaErrorNotSupported;
-  // Two CTAs per SM get ~100 KB of dynamic shared memory each, one CTA ~200 KB.
-  constexpr int B2 = 100 * 1024, B1 = 200 * 1024;
+  // Two CTAs per SM get ~100 KB of dynamic shared memory each.
+  constexpr int B2 = 100 * 1024;
   if (rep)  // one 32-row query, 4 copies in a 128-row tile: a whole document per MMA chain
     return tc::launch_cfg<128, 256, 1, 4, 1, 2, 0>(P, a, bm, s, 2, B2);
   if (rows <= 64) return tc::launch_auto<64, 64, 1, 1, 4, 8>(P, a, bm, s, 2, B2);

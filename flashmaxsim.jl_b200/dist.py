@@ -36,8 +36,11 @@ def shard_range(n_global: int, world: int, rank: int):
 
 
 def candidates_shard_forward(Q, gallery_shard, idxs, qmask, dmask_shard, shard_lo,
-                             normalize=False):
-    """Scores of the slots this shard owns; -Inf elsewhere (fms_candidates_shard_fwd)."""
+                             normalize=False, compact=True):
+    """Scores of the slots this shard owns; -Inf elsewhere (fms_candidates_shard_fwd).
+    compact=True lists the owned slots first and scans only those (a workspace
+    of fms_candidates_shard_workspace_size bytes); False decodes every slot in
+    the scan."""
     if Q.dim() != 3 or gallery_shard.dim() != 3:
         raise DimensionMismatch("candidate layout expects (B, Tq, dim) and (N, Td, dim)")
     B, Tq, dim = Q.shape
@@ -53,9 +56,13 @@ def candidates_shard_forward(Q, gallery_shard, idxs, qmask, dmask_shard, shard_l
     qm = L._mask(qmask, (B, Tq), "qmask")
     dm = L._mask(dmask_shard, (N, Td), "dmask")
     S = torch.empty((B, C), dtype=L.score_dtype(Q.dtype), device=dev)
+    ws, nb = None, 0
+    if compact and Q.dtype != torch.float64:
+        nb = _lib.lib().fms_candidates_shard_workspace_size(B, C)
+        ws = torch.empty(nb, dtype=torch.uint8, device=dev)
     L._run("fms_candidates_shard_fwd", dev, _lib.DTYPE_CODE[Q.dtype], _lib.ptr(Q), _lib.ptr(G),
            _lib.ptr(ix), _lib.ptr(qm), _lib.ptr(dm), dim, Tq, B, Td, N, C, int(shard_lo),
-           int(normalize), _lib.ptr(S))
+           int(normalize), _lib.ptr(S), _lib.ptr(ws), nb)
     return S
 
 
@@ -135,6 +142,115 @@ def gather_packed_scores(S_local, counts, group=None):
     parts = [torch.empty_like(buf) for _ in range(world)]
     dist.all_gather(parts, buf, group=group)
     return torch.cat([p[:, :c] for p, c in zip(parts, counts)], dim=1)
+
+
+# --------------------------------------------------------------------------- C ABI
+
+class Comm:
+    """A communicator of the library's multi-GPU entry points (fms_comm_t): the
+    whole sharded call -- local scan, NCCL exchange, finalisation -- runs in the
+    library on the caller's stream, as a Julia caller would run it through
+    `ccall`.  Made collectively by every rank of a torch.distributed group
+    (rank 0's NCCL unique id is broadcast through the group), on the current
+    device."""
+
+    def __init__(self, handle, nranks, rank):
+        self.handle, self.nranks, self.rank = handle, nranks, rank
+
+    @classmethod
+    def from_group(cls, group=None, device=None):
+        import ctypes as C
+        lib = _lib.lib()
+        if not lib.fms_nccl_available():
+            raise _lib.FMSError("NCCL library not found (libnccl.so.2)")
+        world = dist.get_world_size(group) if dist.is_initialized() else 1
+        rank = dist.get_rank(group) if world > 1 else 0
+        dev = device or torch.device("cuda", torch.cuda.current_device())
+        raw = (C.c_ubyte * 128)()
+        if rank == 0:
+            _lib.check(lib.fms_comm_unique_id(C.cast(raw, C.c_void_p)), "fms_comm_unique_id")
+        if world > 1:
+            backend = dist.get_backend(group)
+            t = torch.tensor(list(raw), dtype=torch.uint8,
+                             device=dev if backend == "nccl" else "cpu")
+            dist.broadcast(t, src=dist.get_global_rank(group, 0) if group else 0, group=group)
+            raw = (C.c_ubyte * 128)(*t.cpu().tolist())
+        h = C.c_void_p()
+        with torch.cuda.device(dev):
+            _lib.check(lib.fms_comm_init(C.byref(h), world, rank, C.cast(raw, C.c_void_p)),
+                       "fms_comm_init")
+        return cls(h, world, rank)
+
+    def close(self):
+        if self.handle is not None:
+            _lib.check(_lib.lib().fms_comm_destroy(self.handle), "fms_comm_destroy")
+            self.handle = None
+
+
+def sharded_candidates_abi(comm, Q, gallery_shard, idxs, qmask, dmask_shard, shard_lo, n_global,
+                           neg=-1.0e4, normalize=False):
+    """fms_sharded_candidates_fwd: the full (B, C) scores on every rank."""
+    B, Tq, dim = Q.shape
+    N, Td = gallery_shard.shape[0], gallery_shard.shape[1]
+    dev = L._device_of(Q, gallery_shard, idxs, qmask, dmask_shard)
+    Q, G = L._feat(Q), L._feat(gallery_shard)
+    ix = L._i32(idxs, "idxs")
+    C = ix.shape[1]
+    qm = L._mask(qmask, (B, Tq), "qmask")
+    dm = L._mask(dmask_shard, (N, Td), "dmask")
+    S = torch.empty((B, C), dtype=torch.float32, device=dev)
+    nb = _lib.lib().fms_sharded_candidates_workspace_size(B, C)
+    ws = torch.empty(nb, dtype=torch.uint8, device=dev)
+    L._run("fms_sharded_candidates_fwd", dev, comm.handle, _lib.DTYPE_CODE[Q.dtype], _lib.ptr(Q),
+           _lib.ptr(G), _lib.ptr(ix), _lib.ptr(qm), _lib.ptr(dm), dim, Tq, B, Td, N, C,
+           int(shard_lo), int(n_global), L._neg_value(neg, Q.dtype), int(normalize),
+           _lib.ptr(S), _lib.ptr(ws), nb)
+    return S
+
+
+def sharded_packed_abi(comm, Qs, P_local, counts, qmask=None, normalize=False):
+    """fms_sharded_packed_fwd: (nq, sum(counts)) scores on every rank; rank r
+    holds the counts[r] documents of P_local (contiguous ranges in rank order)."""
+    import ctypes as C
+    nq, Tq, dim = Qs.shape
+    dev = L._device_of(Qs, P_local.tokens, P_local.cu, qmask)
+    Qs, tok = L._feat(Qs), L._feat(P_local.tokens)
+    cu = L._i32(P_local.cu, "cu")
+    if len(counts) != comm.nranks or counts[comm.rank] != cu.numel() - 1:
+        raise DimensionMismatch("counts[rank] must be this rank's document count")
+    qm = L._mask(qmask, (nq, Tq), "qmask")
+    tot = int(sum(counts))
+    S = torch.empty((nq, tot), dtype=torch.float32, device=dev)
+    nb = _lib.lib().fms_sharded_packed_workspace_size(comm.nranks, nq, max(counts))
+    ws = torch.empty(max(nb, 1), dtype=torch.uint8, device=dev)
+    carr = (C.c_int32 * len(counts))(*[int(c) for c in counts])
+    L._run("fms_sharded_packed_fwd", dev, comm.handle, _lib.DTYPE_CODE[Qs.dtype], _lib.ptr(Qs),
+           _lib.ptr(tok), _lib.ptr(cu), _lib.ptr(qm), dim, Tq, nq, C.cast(carr, C.c_void_p),
+           tok.shape[0], int(normalize), _lib.ptr(S), _lib.ptr(ws), nb)
+    return S
+
+
+def sharded_int8_topk_abi(comm, Q, index_shard, shard_lo, k, qmask=None, dmask_shard=None,
+                          normalize=False, quantized=None):
+    """fms_sharded_int8_topk: (vals (nq, k), ids (nq, k) global 1-based) on every rank."""
+    from .quant import quantize_int8_symmetric, require_int8_index
+    require_int8_index(index_shard)
+    QQ = quantized if quantized is not None else quantize_int8_symmetric(Q)
+    nq, Tq, dim = QQ.codes.shape
+    N, Td = index_shard.codes.shape[0], index_shard.codes.shape[1]
+    dev = L._device_of(QQ.codes, index_shard.codes, qmask, dmask_shard)
+    qm = L._mask(qmask, (nq, Tq), "qmask")
+    dm = L._mask(dmask_shard, (N, Td), "dmask")
+    vals = torch.empty((nq, k), dtype=torch.float32, device=dev)
+    ids = torch.empty((nq, k), dtype=torch.int32, device=dev)
+    nb = _lib.lib().fms_sharded_int8_topk_workspace_size(comm.nranks, nq, N, k)
+    ws = torch.empty(nb, dtype=torch.uint8, device=dev)
+    L._run("fms_sharded_int8_topk", dev, comm.handle, L._scale_code(QQ.scales),
+           L._scale_code(index_shard.scales), _lib.ptr(QQ.codes), _lib.ptr(QQ.scales),
+           _lib.ptr(index_shard.codes.contiguous()), _lib.ptr(index_shard.scales.contiguous()),
+           _lib.ptr(qm), _lib.ptr(dm), dim, Tq, nq, Td, N, int(shard_lo), int(normalize), int(k),
+           _lib.ptr(vals), _lib.ptr(ids), _lib.ptr(ws), nb)
+    return vals, ids
 
 
 def _local_inbatch_forward(Q, D_local, qmask, dmask_local, normalize):

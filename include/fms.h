@@ -52,6 +52,7 @@ enum fms_backward { FMS_ATOMIC_UNIFIED = 0, FMS_INVGRID = 1 };
 #define FMS_ERR_WORKSPACE (-4)   /* workspace missing or too small */
 #define FMS_ERR_UNSUPPORTED (-5) /* no sm_100 device, or feature unavailable */
 #define FMS_ERR_TOO_LARGE (-6)   /* input exceeds a no-allocation entry point's scratch */
+#define FMS_ERR_NCCL (-7)        /* an NCCL call failed (fms_last_nccl_error) */
 
 /* Fixed device scratch of fms_paired_bwd_invgrid_noalloc (bytes). */
 #define FMS_STATIC_SCRATCH_BYTES (4u << 20)
@@ -103,12 +104,17 @@ int fms_candidates_fwd(int dtype, const void* Q, const void* gallery, const int3
    global docs id_lo .. id_lo+N_local-1; slots whose idxs fall outside it get
    -Inf so an all-reduce(max) over shards yields the full S, after which
    fms_candidates_finalize_neg writes `neg` into globally invalid slots.
-   Scores only (float32 / float64 per dtype). */
+   Scores only (float32 / float64 per dtype).  With a workspace of
+   fms_candidates_shard_workspace_size(B, C) bytes the call first lists the
+   slots this shard owns (one pass over idxs, which also writes the -Inf) and
+   scans only those, so its cost does not grow with the number of shards;
+   with workspace NULL every slot is decoded by the scan itself. */
+size_t fms_candidates_shard_workspace_size(int B, int C);
 int fms_candidates_shard_fwd(int dtype, const void* Q, const void* gallery_shard,
                              const int32_t* idxs, const uint8_t* qmask,
                              const uint8_t* dmask_shard, int dim, int Tq, int B, int Td,
                              int64_t N_local, int C, int64_t id_lo, int normalize, void* S,
-                             fms_stream_t stream);
+                             void* workspace, size_t ws_bytes, fms_stream_t stream);
 
 /* Packed cu_seqlens: nq queries Qs (dim,Tq,nq) against the B ragged documents of
    tokens (dim,ntok), doc b = tokens[:, cu[b]:cu[b+1]-1].  S (B,nq), args
@@ -253,6 +259,69 @@ int fms_topk_merge(const float* vals, const int32_t* ids, int k, int nq, int nsh
    all-reduce(max) of S the slots that are invalid globally get `neg`. */
 int fms_candidates_finalize_neg(const int32_t* idxs, int64_t N, int C, int B, double neg,
                                 float* S, fms_stream_t stream);
+
+/* ------------------------------------------------------------ multi-GPU (NCCL)
+   No reference counterpart (the reference is single-device): galleries sharded
+   by document id over the GPUs of one node, one process or task per GPU, each
+   call on the caller's stream doing the local scan, the NCCL exchange and the
+   finalisation, and returning on every rank what the single-device entry point
+   returns for the whole gallery.  NCCL is loaded at run time: the process's
+   own libnccl.so.2 when one is loaded (torch's, NCCL.jl's), else the system's;
+   FMS_NCCL_LIBRARY names another file.  Every rank makes the same calls in the
+   same order (NCCL collectives). */
+typedef struct fms_comm* fms_comm_t;
+#define FMS_UNIQUE_ID_BYTES 128
+
+/* 1 when an NCCL library could be loaded, else 0. */
+int fms_nccl_available(void);
+/* Text of the last NCCL error seen by this thread (static storage). */
+const char* fms_last_nccl_error(void);
+/* An NCCL unique id (FMS_UNIQUE_ID_BYTES bytes): made on one rank and sent to
+   the others by the caller (a file, MPI, a torch.distributed broadcast...). */
+int fms_comm_unique_id(void* id);
+/* Collective over nranks callers: a communicator on the current device. */
+int fms_comm_init(fms_comm_t* comm, int nranks, int rank, const void* id);
+/* Wrap an ncclComm_t the caller created (e.g. NCCL.jl's); not destroyed by
+   fms_comm_destroy. */
+int fms_comm_from_nccl(fms_comm_t* comm, void* nccl_comm);
+int fms_comm_destroy(fms_comm_t comm);
+int fms_comm_size(fms_comm_t comm, int* nranks, int* rank);
+
+/* candidates_forward (forward_layouts.jl:263-290, normalize.jl:37-46) over a
+   gallery sharded by doc id: this rank holds docs id_lo .. id_lo+N_local-1 of
+   N_global.  Lists and scans the slots this rank owns, ncclAllReduce(max) of S
+   (C,B) float32 in place, then `neg` (already T(neg)) in slots outside
+   1:N_global.  Scores only.  Workspace: fms_sharded_candidates_workspace_size. */
+size_t fms_sharded_candidates_workspace_size(int B, int C);
+int fms_sharded_candidates_fwd(fms_comm_t comm, int dtype, const void* Q, const void* gallery_shard,
+                               const int32_t* idxs, const uint8_t* qmask,
+                               const uint8_t* dmask_shard, int dim, int Tq, int B, int Td,
+                               int64_t N_local, int C, int64_t id_lo, int64_t N_global, double neg,
+                               int normalize, float* S, void* workspace, size_t ws_bytes,
+                               fms_stream_t stream);
+
+/* packed_forward (packed.jl:178-217) for nq queries over a packed gallery split
+   into contiguous document ranges: rank r holds counts[r] documents (host array
+   of nranks entries, the same on every rank) with its own 1-based cu_shard.
+   S (B_total, nq) float32 on every rank (ncclAllGather of the score blocks).
+   Workspace: fms_sharded_packed_workspace_size(nranks, nq, max(counts)). */
+size_t fms_sharded_packed_workspace_size(int nranks, int nq, int B_max);
+int fms_sharded_packed_fwd(fms_comm_t comm, int dtype, const void* Qs, const void* tokens_shard,
+                           const int32_t* cu_shard, const uint8_t* qmask, int dim, int Tq, int nq,
+                           const int32_t* counts, int64_t ntok_local, int normalize, float* S,
+                           void* workspace, size_t ws_bytes, fms_stream_t stream);
+
+/* Exhaustive INT8 top-k (the layout of fms_int8_exhaustive_fwd) over an index
+   sharded by doc id (this rank: docs id_lo .. id_lo+N_local-1): local scan and
+   top-k with global ids, ncclAllGather of the (k,nq) lists, device merge (score
+   descending, id ascending).  Workspace: fms_sharded_int8_topk_workspace_size. */
+size_t fms_sharded_int8_topk_workspace_size(int nranks, int nq, int64_t N_local, int k);
+int fms_sharded_int8_topk(fms_comm_t comm, int qs_dtype, int ds_dtype, const int8_t* Qc,
+                          const void* Qs, const int8_t* Gc_shard, const void* Gs_shard,
+                          const uint8_t* qmask, const uint8_t* dmask_shard, int dim, int Tq, int nq,
+                          int Td, int64_t N_local, int64_t id_lo, int normalize, int k,
+                          float* topk_vals, int32_t* topk_ids, void* workspace, size_t ws_bytes,
+                          fms_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -16,7 +16,7 @@ def test_library_exports_every_header_symbol(fms):
     missing = [n for n in names if not hasattr(L, n)]
     assert missing == []
     assert set(names) == set(_lib.SIGNATURES)
-    assert L.fms_version() == 100
+    assert L.fms_version() == 10100
     assert L.fms_status_string(0) == b"ok"
     assert b"invalid" in L.fms_status_string(-1)
 

@@ -28,11 +28,13 @@ def shards_of(N, cuts):
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float32])
 @pytest.mark.parametrize("Tq,Td,dim", [(32, 64, 128), (20, 45, 64)])
-def test_candidates_shards_match_oracle(fms, oracle, dtype, Tq, Td, dim):
+@pytest.mark.parametrize("compact", [True, False])
+def test_candidates_shards_match_oracle(fms, oracle, dtype, Tq, Td, dim, compact):
     """fms_candidates_shard_fwd on three uneven shards, max-combined, then
     fms_candidates_finalize_neg: the full candidate scores.  Invalid slots
     (0, > N, negative), an empty document, a fully masked query row,
-    `normalize` and both `neg = -1e4` and `-Inf`."""
+    `normalize` and both `neg = -1e4` and `-Inf`; with the owned-slot list
+    (compact) and with every slot decoded by the scan."""
     from flashmaxsim_b200 import dist as fd
     rng = seeded(70 + Tq)
     B, C, N = 5, 60, 53
@@ -55,7 +57,7 @@ def test_candidates_shards_match_oracle(fms, oracle, dtype, Tq, Td, dim):
             S = None
             for lo, hi in parts:
                 Sl = fd.candidates_shard_forward(Q, G[lo - 1:hi], ix, qm, dm[lo - 1:hi], lo,
-                                                 normalize=norm)
+                                                 normalize=norm, compact=compact)
                 # slots outside this shard are exactly -Inf
                 own = (ix >= lo) & (ix <= hi)
                 assert torch.isneginf(Sl[~own]).all()
@@ -124,3 +126,41 @@ def test_int8_topk_shards_match_oracle(fms, oracle):
             kth = float(vo[r, -1])
             for j in got ^ ref:
                 assert abs(float(So[r, j - 1]) - kth) <= 1e-5 * max(1.0, abs(kth))
+
+
+@pytest.fixture(scope="module")
+def comm1(fms):
+    """A one-rank communicator of the library's NCCL entry points."""
+    from flashmaxsim_b200 import dist as fd
+    c = fd.Comm.from_group()
+    yield c
+    c.close()
+
+
+def test_sharded_abi_single_rank(fms, oracle, comm1):
+    """The NCCL entry points with one rank (the whole gallery is the shard): the
+    same results as the single-device entry points and the oracle."""
+    from flashmaxsim_b200 import dist as fd
+    rng = seeded(73)
+    B, C, N, Tq, Td, dim = 4, 90, 41, 32, 70, 128
+    Q = feats(rng, (B, Tq, dim), torch.float16)
+    G = feats(rng, (N, Td, dim), torch.float16)
+    lens = rng.integers(0, Td + 1, N)
+    dm = torch.from_numpy(np.arange(Td)[None, :] < lens[:, None]).cuda()
+    idxs = rng.integers(-1, N + 3, (B, C)).astype(np.int32)
+    ix = torch.from_numpy(idxs).cuda()
+    for neg in (-1.0e4, float("-inf")):
+        S = fd.sharded_candidates_abi(comm1, Q, G, ix, None, dm, 1, N, neg=neg, normalize=True)
+        So, _ = oracle.candidates(Q, G, idxs, None, dm.cpu(), neg=neg, normalize=True)
+        assert_scores(S.cpu(), So, 1e-3)
+    lensp = [int(x) for x in rng.integers(0, 200, 17)]
+    P = fms.pack_docs([feats(rng, (n, dim), torch.float16) for n in lensp])
+    Qs = feats(rng, (3, 24, dim), torch.float16)
+    Sp = fd.sharded_packed_abi(comm1, Qs, P, [len(lensp)])
+    Spo, _ = oracle.packed(Qs, P.tokens, P.cu.cpu())
+    assert_scores(Sp.cpu(), Spo, 1e-3)
+    Gi = fms.quantize_int8_symmetric(feats(rng, (300, 128, dim), torch.float32))
+    Qi = feats(rng, (5, 32, dim), torch.float16)
+    v, i = fd.sharded_int8_topk_abi(comm1, Qi, Gi, 1, 20)
+    fv, fi = fms.int8_exhaustive_forward(Qi, Gi, topk=20)
+    assert torch.equal(i, fi) and torch.equal(v, fv)
