@@ -3,8 +3,10 @@
 // Each entry point checks its arguments the way the reference's layout drivers
 // do (require_*_shapes raise DimensionMismatch / ArgumentError; here they return
 // FMS_ERR_INVALID), builds the shared ScanParams geometry and dispatches:
-// 16-bit features go to the tcgen05 + TMA engine when its TMA constraints hold,
-// everything else (and Float32 / Float64) to the CUDA-core scan.  No entry
+// 16-bit features go to a tcgen05 + TMA engine when its constraints hold (the
+// short-query gallery engine for paired / candidate layouts with Tq <= 32 and
+// dim <= 256, else the general engine), everything else (and Float32 /
+// Float64) to the CUDA-core scan.  No entry
 // point allocates, synchronizes, prints or aborts.
 #include <cuda.h>
 #include <mutex>
@@ -61,6 +63,10 @@ static size_t elem_size(int dtype) {
 static int run_scan(int dtype, ScanParams& p, cudaStream_t s) {
   p.nunits = num_units(p);
   if (p.nunits == 0) return FMS_OK;
+  if ((dtype == FMS_F16 || dtype == FMS_BF16) && scan_gallery_supported(dtype, p)) {
+    cudaError_t e = launch_scan_gallery(dtype, p, s);
+    if (e != cudaErrorNotSupported) return status_of(e);
+  }
   if ((dtype == FMS_F16 || dtype == FMS_BF16) && scan_tc_supported(dtype, p)) {
     cudaError_t e = launch_scan_tc(dtype, p, s);
     if (e != cudaErrorNotSupported) return status_of(e);
@@ -99,7 +105,8 @@ int fms_version(void) { return 10100; }
 int fms_device_error(int reset) {
   const int a = read_device_error(reset);
   const int b = read_i8tc_device_error(reset);
-  return a != 0 ? a : b;
+  const int c = read_gal_device_error(reset);
+  return a != 0 ? a : (b != 0 ? b : c);
 }
 
 int fms_pair_fwd(int dtype, const void* q, const void* d, const uint8_t* qmask,

@@ -2,6 +2,7 @@
 // the C-ABI layer (fms_abi.cu).  Not part of the public ABI.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -23,6 +24,14 @@ cudaError_t launch_scan_tc(int dtype, const ScanParams& p, cudaStream_t s);
 bool scan_tc_supported(int dtype, const ScanParams& p);
 // Device health flag set by engine waits that timed out (0 = healthy).
 int read_device_error(int reset);
+// 2-D TMA map over a token matrix (dim, rows) of 16-bit elements (fmt 0 = f16,
+// 1 = bf16): boxes of 64 elements x box_rows rows, 128-byte swizzle.
+bool make_tmap_16(CUtensorMap* m, const void* base, uint32_t fmt, int dim, int64_t rows, int box_rows);
+// The short-query gallery engine (fms_scan_gallery.cu): paired and candidate
+// layouts with Tq <= 32, document tokens on the MMA M side.
+bool scan_gallery_supported(int dtype, const ScanParams& p);
+cudaError_t launch_scan_gallery(int dtype, const ScanParams& p, cudaStream_t s);
+int read_gal_device_error(int reset);
 
 cudaError_t launch_inv_counts(int dtype, const uint8_t* qmask, int Tq, int B, void* inv_n,
                               cudaStream_t s);

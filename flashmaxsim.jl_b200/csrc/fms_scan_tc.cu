@@ -856,6 +856,10 @@ static cudaError_t launch_auto(const TcParams& P, const CUtensorMap& a, const BM
 
 }  // namespace tc
 
+bool make_tmap_16(CUtensorMap* m, const void* base, uint32_t fmt, int dim, int64_t rows, int box_rows) {
+  return tc::make_map(m, base, fmt, dim, rows, box_rows);
+}
+
 int read_device_error(int reset) {
   int v = 0;
   cudaError_t e = cudaMemcpyFromSymbol(&v, g_tc_error, sizeof(int));
