@@ -14,11 +14,13 @@ from .layouts import (candidates_forward, candidates_pullback, inbatch_forward, 
                       varlen_pullback)
 from .packed import PackedSeq, make_packed, nseq, pack_docs, pack_pairs
 from .quant import Int8Index, dequant_int8, quantize_int8_symmetric
+from .store import load_int8_index, load_packed, save_int8_index, save_packed
 from ._lib import FMSError, lib as load_library
 
 __all__ = [
     "MaxSim", "InBatch", "BackwardStrategy", "AtomicUnified", "InvGrid",
     "maxsim", "maxsim_dense", "score_eltype",
     "pack_docs", "pack_pairs", "PackedSeq", "nseq", "Int8Index", "quantize_int8_symmetric",
+    "save_int8_index", "load_int8_index", "save_packed", "load_packed",
     "DimensionMismatch", "ArgumentError", "FMSError",
 ]

@@ -5,7 +5,8 @@
 // single-device layout driver returns for the whole gallery.
 //
 //  * Candidates: a compaction kernel reads the (C, B) idxs once, lists the slots
-//    whose document this shard holds and writes -Inf into every other slot; the
+//    whose document this shard holds (in order within 8192-slot ranges) and
+//    writes -Inf into every other slot; the
 //    scan walks only the list (per-rank work independent of the number of
 //    ranks); ncclAllReduce(max) merges the owner-disjoint scores in place and
 //    the `neg` fill of globally invalid slots follows.
@@ -96,29 +97,63 @@ static int nccl_status(ncclResult_t r) {
 // ------------------------------------------------------------------ kernels
 
 // Candidate slots of this shard: unit u (= b * C + c) is owned when idxs[u] is
-// one of the shard's documents id_lo .. id_lo + n_local - 1.  Owned units are
-// appended to `list` (a warp's 32 units in order, warps in any order: every
-// unit's output is independent, so the order changes nothing in the results);
-// the others get -Inf, which loses the max-merge.
-__global__ void shard_compact_kernel(const int32_t* __restrict__ idxs, int64_t n, int64_t id_lo,
-                                     int64_t n_local, int32_t* __restrict__ list,
-                                     int32_t* __restrict__ count, float* __restrict__ S) {
-  const int lane = threadIdx.x & 31;
-  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  for (int64_t u0 = warp * 32; u0 < n; u0 += nwarps * 32) {
-    const int64_t u = u0 + lane;
-    bool own = false;
-    if (u < n) {
-      const int64_t j = (int64_t)idxs[u] - (id_lo - 1);
-      own = j >= 1 && j <= n_local;
-      if (!own) S[u] = -INFINITY;
+// one of the shard's documents id_lo .. id_lo + n_local - 1.  A block takes a
+// contiguous range of COMPACT_TILE units, lists its owned units in order into
+// one reserved output range (one atomic per block), so the list keeps runs of
+// the same query together (the scan reloads its query tile only when the
+// query changes); blocks land in any order, which changes nothing in the
+// results (every unit's output is independent).  The other units get -Inf,
+// which loses the max-merge.
+constexpr int COMPACT_THREADS = 1024;
+constexpr int COMPACT_ITEMS = 8;
+constexpr int COMPACT_TILE = COMPACT_THREADS * COMPACT_ITEMS;
+
+__global__ void __launch_bounds__(COMPACT_THREADS)
+shard_compact_kernel(const int32_t* __restrict__ idxs, int64_t n, int64_t id_lo, int64_t n_local,
+                     int32_t* __restrict__ list, int32_t* __restrict__ count, float* __restrict__ S) {
+  __shared__ int32_t warp_tot[COMPACT_THREADS / 32];
+  __shared__ int32_t base_s;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  for (int64_t t0 = (int64_t)blockIdx.x * COMPACT_TILE; t0 < n; t0 += (int64_t)gridDim.x * COMPACT_TILE) {
+    // thread k holds units t0 + k*ITEMS .. + ITEMS-1 (consecutive, in order)
+    const int64_t u0 = t0 + (int64_t)threadIdx.x * COMPACT_ITEMS;
+    uint32_t own = 0u;
+#pragma unroll
+    for (int j = 0; j < COMPACT_ITEMS; ++j) {
+      const int64_t u = u0 + j;
+      if (u < n) {
+        const int64_t d = (int64_t)idxs[u] - (id_lo - 1);
+        if (d >= 1 && d <= n_local) own |= 1u << j;
+        else S[u] = -INFINITY;
+      }
     }
-    const uint32_t m = __ballot_sync(0xffffffffu, own);
-    int base = 0;
-    if (lane == 0 && m != 0u) base = atomicAdd(count, __popc(m));
-    base = __shfl_sync(0xffffffffu, base, 0);
-    if (own) list[base + __popc(m & ((1u << lane) - 1u))] = (int32_t)u;
+    const int cnt = __popc(own);
+    // block-wide exclusive scan of the per-thread counts
+    int incl = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    if (lane == 31) warp_tot[w] = incl;
+    __syncthreads();
+    if (w == 0) {
+      const int t = warp_tot[lane];
+      int wi = t;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, wi, o);
+        if (lane >= o) wi += v;
+      }
+      warp_tot[lane] = wi - t;  // exclusive offset of each warp
+      if (lane == 31) base_s = wi > 0 ? atomicAdd(count, wi) : 0;
+    }
+    __syncthreads();
+    int pos = base_s + warp_tot[w] + incl - cnt;
+#pragma unroll
+    for (int j = 0; j < COMPACT_ITEMS; ++j)
+      if ((own >> j) & 1u) list[pos++] = (int32_t)(u0 + j);
+    __syncthreads();  // warp_tot / base_s are rewritten by the next tile
   }
 }
 
@@ -163,8 +198,11 @@ cudaError_t launch_shard_compact(const int32_t* idxs, int64_t nslots, int64_t id
   cudaError_t e = cudaMemsetAsync(cnt, 0, 4, s);
   if (e != cudaSuccess) return e;
   if (nslots > 0) {
-    shard_compact_kernel<<<grid_for(nslots, 256), 256, 0, s>>>(idxs, nslots, id_lo, n_local, lst,
-                                                                cnt, S);
+    int64_t blocks = (nslots + COMPACT_TILE - 1) / COMPACT_TILE;
+    const int64_t cap = (int64_t)device_sm_count() * 2;
+    if (blocks > cap) blocks = cap;
+    shard_compact_kernel<<<(unsigned)blocks, COMPACT_THREADS, 0, s>>>(idxs, nslots, id_lo, n_local,
+                                                                       lst, cnt, S);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   *list = lst;

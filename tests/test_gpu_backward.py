@@ -223,3 +223,29 @@ def test_invgrid_long_segments_deterministic(fms, oracle, dtype):
                                           1, dcode)
     close(r1[0], dQo, tol, "cand dQ")
     close(r1[1], dGo, tol, "cand dG")
+
+
+def test_candidates_invgrid_million_destinations(fms, oracle):
+    """Candidate InvGrid pullback at scale (csr_ka.jl:53-65 builds this CSR with
+    one thread): 4,000 documents x 256 tokens = 1.02 M destinations, 16 queries
+    x 500 candidates x 32 tokens = 256 k sources, bf16 features with prefix
+    masks and invalid slots; the block-parallel CSR must give the oracle's
+    ascending-order sums, and two runs must agree bit for bit."""
+    rng = seeded(49)
+    B, C, Tq, Td, N, dim = 16, 500, 32, 256, 4000, 128
+    dtype = torch.bfloat16
+    Q = feats(rng, (B, Tq, dim), dtype)
+    G = feats(rng, (N, Td, dim), dtype)
+    lens = rng.integers(64, Td + 1, N)
+    dm = torch.from_numpy(np.arange(Td)[None, :] < lens[:, None]).cuda()
+    idxs = rng.integers(1, N + 1, (B, C)).astype(np.int32)
+    idxs[rng.random((B, C)) < 0.02] = 0
+    ix = torch.from_numpy(idxs).cuda()
+    _, args = fms.candidates_forward(Q, G, ix, None, dm)
+    Delta = torch.randn(B, C, device="cuda")
+    dQ, dG = fms.candidates_pullback(Delta, Q, G, ix, None, args, None, fms.InvGrid())
+    dQ2, dG2 = fms.candidates_pullback(Delta, Q, G, ix, None, args, None, fms.InvGrid())
+    assert torch.equal(dG, dG2) and torch.equal(dQ, dQ2)
+    dQo, dGo = oracle.candidates_pullback(Delta.to(dtype), None, Q, G, idxs, None, args.cpu(), 1, 2)
+    close(dQ, dQo, 1e-2, "dQ")
+    close(dG, dGo, 1e-2, "dG")
