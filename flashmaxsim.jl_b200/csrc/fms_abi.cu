@@ -466,7 +466,10 @@ int fms_int8_paired_fwd(int qs_dtype, int ds_dtype, const int8_t* Qc, const void
   p.qs_dtype = qs_dtype; p.ds_dtype = ds_dtype;
   p.dim = dim; p.Tq = Tq; p.Td = Td; p.exhaustive = 0; p.N = B; p.nunits = B;
   p.normalize = normalize; p.scores = scores; p.args = args;
-  return status_of(launch_int8_scan(p, (cudaStream_t)stream));
+  // tensor cores (kind::i8) when the shape allows, else the dp4a scan
+  cudaError_t e = launch_int8_paired_tc(p, (cudaStream_t)stream);
+  if (e == cudaErrorNotSupported) e = launch_int8_scan(p, (cudaStream_t)stream);
+  return status_of(e);
 }
 
 int fms_int8_pair_fwd(int qs_dtype, int ds_dtype, const int8_t* qc, const void* qs,

@@ -30,6 +30,10 @@ cudaError_t launch_int8_scan(const Int8ScanParams& p, cudaStream_t s);
 // or above 256, Tq > 32, Td > 256, unaligned codes, no tape); the caller then
 // runs the SIMT scan, which is also a GPU kernel.
 bool int8_exhaustive_tc_supported(const Int8ScanParams& p);
+// The short-query gallery engine's INT8 kind for the paired layout (pair is B = 1):
+// Tq <= 32, dim 128 or 256, codes 16-byte aligned (fms_scan_gallery.cu).
+bool int8_paired_tc_supported(const Int8ScanParams& p);
+cudaError_t launch_int8_paired_tc(const Int8ScanParams& p, cudaStream_t s);
 cudaError_t launch_int8_exhaustive_tc(const Int8ScanParams& p, cudaStream_t s);
 int read_i8tc_device_error(int reset);
 size_t topk_workspace_bytes(int nq, int64_t N, int k);

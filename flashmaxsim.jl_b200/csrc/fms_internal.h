@@ -27,6 +27,8 @@ int read_device_error(int reset);
 // 2-D TMA map over a token matrix (dim, rows) of 16-bit elements (fmt 0 = f16,
 // 1 = bf16): boxes of 64 elements x box_rows rows, 128-byte swizzle.
 bool make_tmap_16(CUtensorMap* m, const void* base, uint32_t fmt, int dim, int64_t rows, int box_rows);
+// The same over int8 token rows: boxes of 128 elements (128 bytes) x box_rows.
+bool make_tmap_i8(CUtensorMap* m, const void* base, int dim, int64_t rows, int box_rows);
 // The short-query gallery engine (fms_scan_gallery.cu): paired and candidate
 // layouts with Tq <= 32, document tokens on the MMA M side.
 bool scan_gallery_supported(int dtype, const ScanParams& p);

@@ -44,6 +44,7 @@
 #include <cuda.h>
 
 #include "fms_common.cuh"
+#include "fms_int8.cuh"
 #include "fms_internal.h"
 #include "fms_tc_ptx.cuh"
 
@@ -62,22 +63,30 @@ constexpr int NGROUP = 2;    // epilogue groups (alternate units)
 constexpr int NEPI = 4 * NGROUP;  // epilogue warps (a group: one per TMEM subpartition)
 constexpr int NWARPS = EPI_WARP0 + NEPI;
 constexpr int NTHREADS = NWARPS * 32;
-constexpr int CTAS_PER_SM = 2;            // two independent pipelines per SM
-constexpr int TMEM_COLS = 512 / CTAS_PER_SM;
+// Per element kind: 16-bit features run two independent pipelines (CTAs) per
+// SM; INT8 codes one (the dequantisation keeps 32 query scales in registers).
+template <bool I8> struct Kind {
+  static constexpr int CTAS_PER_SM = I8 ? 1 : 2;
+  static constexpr int TMEM_COLS = 512 / CTAS_PER_SM;
+  static constexpr int SMEM_BUDGET = I8 ? 212 * 1024 : 106 * 1024;  // dynamic, per CTA
+};
 constexpr int UQ = 16;       // metadata ring depth
 constexpr int MW_MAX = 16;   // document mask words held per unit (32 * 16 = 512 tokens)
 constexpr int SMAX = 4;      // document slots at most
-constexpr int NACC_MAX = TMEM_COLS / 32;  // accumulators at most
+constexpr int NACC_MAX = 512 / 32;  // accumulators at most
 
 struct Params {
   ScanParams p;
-  int KB;          // dim / 64
-  uint32_t fmt;    // 0 = f16, 1 = bf16
+  const void* qs;  // INT8: query token scales (Tq per query), f32 or f16
+  const void* ds;  // INT8: document token scales (one per document row)
+  int qs_f16, ds_f16;
+  int KB;          // 128-byte K blocks per row (dim / 64 for 16-bit, dim / 128 for INT8)
+  uint32_t fmt;    // 16-bit kinds: 0 = f16, 1 = bf16
   int slot_rows;   // document rows per chunk (256 or 128)
   int sr_log2;     // log2(slot_rows)
   int nslots;      // shared-memory slots
   int acc_cols;    // TMEM columns per chunk (slot_rows / 128 * 32)
-  int nacc;        // accumulators (TMEM_COLS / acc_cols)
+  int nacc;        // accumulators (TMEM columns / acc_cols)
   int qslots;      // resident query tiles (1 or 2)
 };
 
@@ -191,8 +200,13 @@ __device__ __forceinline__ void rs_argmax(float (&v)[32], int (&a)[32], int lane
   ao = a[0];
 }
 
-template <bool ARGS>
-__global__ void __launch_bounds__(NTHREADS, CTAS_PER_SM)
+__device__ __forceinline__ float ld_scale(const void* p, int f16, int64_t i) {
+  return f16 ? __half2float(__ldg(static_cast<const __half*>(p) + i))
+             : __ldg(static_cast<const float*>(p) + i);
+}
+
+template <bool ARGS, bool I8>
+__global__ void __launch_bounds__(NTHREADS, Kind<I8>::CTAS_PER_SM)
 gallery_kernel(const __grid_constant__ Maps maps, Params P) {
   extern __shared__ __align__(1024) unsigned char dsm[];
   __shared__ __align__(8) uint64_t full_bar[SMAX];
@@ -250,6 +264,8 @@ gallery_kernel(const __grid_constant__ Maps maps, Params P) {
     ptx::prefetch_tmap(&maps.b32);
     ptx::prefetch_tmap(&maps.b16);
   }
+  constexpr int TMEM_COLS = Kind<I8>::TMEM_COLS;
+  constexpr int KBLK_E = I8 ? 128 : KBLK;  // elements per 128-byte K block
   if (warp == MMA_WARP) ptx::tmem_alloc(&tmem_base_s, TMEM_COLS);
   ptx::tc_fence_before();
   __syncthreads();
@@ -370,7 +386,7 @@ gallery_kernel(const __grid_constant__ Maps maps, Params P) {
           if (!ptx::mbar_wait(&aempty_bar[qs], qphase ^ 1, &abort_s)) goto prod_out;
           ptx::mbar_expect_tx(&afull_bar[qs], (uint32_t)qslot_bytes);
           for (int kb = 0; kb < P.KB; ++kb)
-            ptx::tma_load_2d(qslots + qs * qslot_bytes + kb * QTILE, &maps.q, kb * KBLK, (int)q_row0,
+            ptx::tma_load_2d(qslots + qs * qslot_bytes + kb * QTILE, &maps.q, kb * KBLK_E, (int)q_row0,
                              &afull_bar[qs]);
         }
         const int nch = (leff + SR - 1) >> P.sr_log2;
@@ -381,7 +397,7 @@ gallery_kernel(const __grid_constant__ Maps maps, Params P) {
           unsigned char* st = ring + slot * slot_bytes;
           ptx::mbar_expect_tx(&full_bar[slot], (uint32_t)(P.KB * nr * ROWB));
           for (int kb = 0; kb < P.KB; ++kb)
-            load_rows(st + kb * SR * ROWB, &maps.b128, &maps.b64, &maps.b32, &maps.b16, kb * KBLK,
+            load_rows(st + kb * SR * ROWB, &maps.b128, &maps.b64, &maps.b32, &maps.b16, kb * KBLK_E,
                       d_row0 + (int64_t)c * SR, nr, &full_bar[slot]);
           if (++slot == P.nslots) { slot = 0; sphase ^= 1u; }
         }
@@ -397,7 +413,7 @@ gallery_kernel(const __grid_constant__ Maps maps, Params P) {
       bool holding = false;
       int slot = 0, acc = 0;           // slot and accumulator of the next chunk
       uint32_t sphase = 0, aphase = 0; // parities of their uses
-      const uint32_t idesc = ptx::idesc_f16(P.fmt, 128, NQ);
+      const uint32_t idesc = I8 ? ptx::idesc_i8(128, NQ) : ptx::idesc_f16(P.fmt, 128, NQ);
       for (int64_t i = 0;; ++i) {
         const int ms = (int)(i % UQ);
         if (!ptx::mbar_wait(&metaf_bar[ms], (uint32_t)((i / UQ) & 1), &abort_s)) goto mma_out;
@@ -428,9 +444,12 @@ gallery_kernel(const __grid_constant__ Maps maps, Params P) {
             for (int kb = 0; kb < P.KB; ++kb) {
               const uint64_t adesc = ptx::sw128_desc(sbase + (uint32_t)(kb * SR * ROWB + t * 128 * ROWB));
               const uint64_t bdesc = ptx::sw128_desc(qbase + (uint32_t)(kb * QTILE));
+              // four 32-byte K steps per block (K = 16 f16 / bf16, K = 32 int8)
 #pragma unroll
-              for (int k = 0; k < KBLK / 16; ++k)
-                ptx::mma_f16(d, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0);
+              for (int k = 0; k < 4; ++k) {
+                if (I8) ptx::mma_i8(d, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0);
+                else ptx::mma_f16(d, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0);
+              }
             }
           }
           ptx::mma_commit(&empty_bar[slot]);
@@ -468,6 +487,13 @@ gallery_kernel(const __grid_constant__ Maps maps, Params P) {
       const int first = m.first;
       float mx = -INFINITY;
       int ag = 0;
+      // INT8: the unit's 32 query-token scales, one per lane, then in every lane
+      float qsr[I8 ? 32 : 1];
+      if (I8) {
+        const float q_own = lane < m.Tq ? ld_scale(P.qs, P.qs_f16, m.q_row0 + lane) : 0.f;
+#pragma unroll
+        for (int j = 0; j < (I8 ? 32 : 1); ++j) qsr[j] = __shfl_sync(0xffffffffu, q_own, j);
+      }
       for (int c = 0; c < nch; ++c) {
         const int n = min(SR, leff - c * SR);
         const int ntile = (n + 127) >> 7;
@@ -491,6 +517,14 @@ gallery_kernel(const __grid_constant__ Maps maps, Params P) {
                              (uint32_t)(t * NQ),
                          r);
           ptx::tmem_wait_ld();
+          if (I8) {
+            // s = (qs_t * ds_u) * float(acc): acc is the exact int32 dot product
+            // (quant.jl:113), exactly representable (|acc| < 2^24 for dim <= 1024)
+            const float dsu = (u < leff) ? ld_scale(P.ds, P.ds_f16, m.d_row0 + u) : 0.f;
+#pragma unroll
+            for (int j = 0; j < (I8 ? 32 : 1); ++j)
+              r[j] = __float_as_uint((qsr[j] * dsu) * __int2float_rn((int)r[j]));
+          }
           if (u == first) {
 #pragma unroll
             for (int j = 0; j < 32; ++j) s0_s[g][par][j] = __uint_as_float(r[j]);
@@ -552,9 +586,17 @@ gallery_kernel(const __grid_constant__ Maps maps, Params P) {
           if (s0 != s0) val = s0;
           okr = tv;
         }
-        float sum = okr ? val : 0.f;
+        const float rowv = okr ? val : 0.f;
+        float sum = 0.f;
+        if (I8) {
+          // Sigma_t in t order (quant.jl:121-123), so INT8 scores are the
+          // reference's bit for bit
+          for (int tt = 0; tt < m.Tq; ++tt) sum += __shfl_sync(0xffffffffu, rowv, tt);
+        } else {
+          sum = rowv;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+          for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        }
         if (lane == 0) {
           if (p.normalize) {
             const int nvalid = __popc(m.qw & (m.Tq >= 32 ? 0xffffffffu : ((1u << m.Tq) - 1u)));
@@ -585,10 +627,6 @@ done:
   }
 }
 
-// dynamic shared memory per CTA: two CTAs per SM share its 228 KB with their
-// static shared memory (~5 KB each) and the 1 KB the system reserves per CTA
-constexpr int SMEM_BUDGET = 106 * 1024;
-
 }  // namespace gal
 
 int read_gal_device_error(int reset) {
@@ -605,45 +643,69 @@ int read_gal_device_error(int reset) {
 
 // Slot rows, accumulators, resident query tiles and slots of one CTA: two
 // query tiles when three document slots still fit beside them, else one (a
-// query change then waits for the previous query's last MMA).
-static void gal_plan(const ScanParams& p, gal::Params& P) {
-  P.KB = p.dim / gal::KBLK;
-  P.slot_rows = P.KB == 1 ? 256 : 128;
-  P.sr_log2 = P.KB == 1 ? 8 : 7;
+// query change then waits for the previous query's last MMA).  16-bit kinds
+// share the SM with a second CTA (106 KB, 256 TMEM columns each).
+template <bool I8>
+static void gal_plan(int dim, gal::Params& P) {
+  using K = gal::Kind<I8>;
+  P.KB = I8 ? dim / 128 : dim / gal::KBLK;
+  P.slot_rows = (I8 || P.KB == 1) ? 256 : 128;
+  P.sr_log2 = P.slot_rows == 256 ? 8 : 7;
   P.acc_cols = (P.slot_rows / 128) * gal::NQ;
-  P.nacc = gal::TMEM_COLS / P.acc_cols;
+  P.nacc = K::TMEM_COLS / P.acc_cols;
   if (P.nacc > gal::NACC_MAX) P.nacc = gal::NACC_MAX;
   const int slot_bytes = P.KB * P.slot_rows * gal::ROWB;
   for (P.qslots = 2; P.qslots >= 1; --P.qslots) {
-    P.nslots = (gal::SMEM_BUDGET - 1024 - P.qslots * P.KB * gal::QTILE) / slot_bytes;
+    P.nslots = (K::SMEM_BUDGET - 1024 - P.qslots * P.KB * gal::QTILE) / slot_bytes;
     if (P.nslots >= 3 || P.qslots == 1) break;
   }
   if (P.nslots > gal::SMAX) P.nslots = gal::SMAX;
 }
 
-bool scan_gallery_supported(int dtype, const ScanParams& p) {
-  if (dtype != FMS_F16 && dtype != FMS_BF16) return false;
-  if (p.layout != L_PAIRED && p.layout != L_CANDIDATES) return false;
+// Shapes both kinds take: paired / candidate units of at most 32 query tokens,
+// token rows addressable by TMA, at most nacc - 1 chunks per unit (an epilogue
+// group then never waits on an accumulator whose previous use, by the other
+// group, is still uncommitted -- a parity wait could not tell the two apart).
+template <bool I8>
+static bool gal_shape_ok(const ScanParams& p) {
   if (device_cc() != 100) return false;
+  if (p.layout != L_PAIRED && p.layout != L_CANDIDATES) return false;
   if (p.Tq < 1 || p.Tq > gal::NQ) return false;
-  if (p.dim < 64 || p.dim > 256 || p.dim % gal::KBLK != 0) return false;
   if (p.nq_tok <= 0 || p.nd_tok <= 0 || p.nq_tok >= INT32_MAX || p.nd_tok >= INT32_MAX) return false;
   if ((reinterpret_cast<uintptr_t>(p.Q) & 15) || (reinterpret_cast<uintptr_t>(p.D) & 15)) return false;
   gal::Params P;
-  gal_plan(p, P);
-  // At most nacc - 1 chunks per unit: an epilogue group then never waits on an
-  // accumulator whose previous use (by the other group) is still uncommitted,
-  // which a parity-based wait could not tell from the use it wants.
+  gal_plan<I8>(p.dim, P);
   if (p.Td > (P.nacc - 1) * P.slot_rows) return false;
   return P.nslots >= 2;
+}
+
+bool scan_gallery_supported(int dtype, const ScanParams& p) {
+  if (dtype != FMS_F16 && dtype != FMS_BF16) return false;
+  if (p.dim < 64 || p.dim > 256 || p.dim % gal::KBLK != 0) return false;
+  return gal_shape_ok<false>(p);
+}
+
+template <bool I8>
+static cudaError_t gal_launch(gal::Params& P, const gal::Maps& maps, cudaStream_t s) {
+  const ScanParams& p = P.p;
+  const int dyn = P.qslots * P.KB * gal::QTILE + P.nslots * P.KB * P.slot_rows * gal::ROWB + 1024;
+  auto k = p.args ? gal::gallery_kernel<true, I8> : gal::gallery_kernel<false, I8>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn);
+  if (e != cudaSuccess) return e;
+  int64_t grid = (int64_t)device_sm_count() * gal::Kind<I8>::CTAS_PER_SM;
+  if (grid > p.nunits) grid = p.nunits;
+  if (grid < 1) grid = 1;
+  k<<<(unsigned)grid, gal::NTHREADS, dyn, s>>>(maps, P);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_scan_gallery(int dtype, const ScanParams& p, cudaStream_t s) {
   if (!scan_gallery_supported(dtype, p)) return cudaErrorNotSupported;
   gal::Params P;
+  memset(&P, 0, sizeof(P));
   P.p = p;
   P.fmt = dtype == FMS_BF16 ? 1u : 0u;
-  gal_plan(p, P);
+  gal_plan<false>(p.dim, P);
   if (p.nunits == 0) return cudaSuccess;
   gal::Maps maps;
   if (!make_tmap_16(&maps.q, p.Q, P.fmt, p.dim, p.nq_tok, gal::NQ) ||
@@ -652,15 +714,48 @@ cudaError_t launch_scan_gallery(int dtype, const ScanParams& p, cudaStream_t s) 
       !make_tmap_16(&maps.b32, p.D, P.fmt, p.dim, p.nd_tok, 32) ||
       !make_tmap_16(&maps.b16, p.D, P.fmt, p.dim, p.nd_tok, 16))
     return cudaErrorNotSupported;
-  const int dyn = P.qslots * P.KB * gal::QTILE + P.nslots * P.KB * P.slot_rows * gal::ROWB + 1024;
-  auto k = p.args ? gal::gallery_kernel<true> : gal::gallery_kernel<false>;
-  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn);
-  if (e != cudaSuccess) return e;
-  int64_t grid = (int64_t)device_sm_count() * gal::CTAS_PER_SM;
-  if (grid > p.nunits) grid = p.nunits;
-  if (grid < 1) grid = 1;
-  k<<<(unsigned)grid, gal::NTHREADS, dyn, s>>>(maps, P);
-  return cudaGetLastError();
+  return gal_launch<false>(P, maps, s);
+}
+
+// INT8 pair / paired (int8_pair_forward_host, quant.jl:96-125; the reference's
+// GPU path is the s8 WMMA kernel at ext/FlashMaxSimCUDAExt.jl:621-746): codes
+// on the tensor cores (kind::i8), the pair formula in the epilogue.
+static ScanParams i8_scan_params(const Int8ScanParams& ip) {
+  ScanParams p;
+  memset(&p, 0, sizeof(p));
+  p.layout = L_PAIRED;
+  p.Q = ip.Qc; p.D = ip.Dc; p.qmask = ip.qmask; p.dmask = ip.dmask;
+  p.dim = ip.dim; p.Tq = ip.Tq; p.Td = ip.Td; p.B = (int)ip.N;
+  p.nq_tok = (int64_t)ip.Tq * ip.N; p.nd_tok = (int64_t)ip.Td * ip.N;
+  p.nunits = ip.N;
+  p.normalize = ip.normalize; p.scores = ip.scores; p.args = ip.args;
+  return p;
+}
+
+bool int8_paired_tc_supported(const Int8ScanParams& ip) {
+  if (ip.exhaustive) return false;
+  if (ip.dim % 128 != 0 || ip.dim < 128 || ip.dim > 256) return false;
+  if (ip.N < 1 || ip.N >= INT32_MAX) return false;
+  return gal_shape_ok<true>(i8_scan_params(ip));
+}
+
+cudaError_t launch_int8_paired_tc(const Int8ScanParams& ip, cudaStream_t s) {
+  if (!int8_paired_tc_supported(ip)) return cudaErrorNotSupported;
+  gal::Params P;
+  memset(&P, 0, sizeof(P));
+  P.p = i8_scan_params(ip);
+  P.qs = ip.Qs; P.ds = ip.Ds;
+  P.qs_f16 = ip.qs_dtype == FMS_F16; P.ds_f16 = ip.ds_dtype == FMS_F16;
+  gal_plan<true>(ip.dim, P);
+  gal::Maps maps;
+  const ScanParams& p = P.p;
+  if (!make_tmap_i8(&maps.q, p.Q, p.dim, p.nq_tok, gal::NQ) ||
+      !make_tmap_i8(&maps.b128, p.D, p.dim, p.nd_tok, 128) ||
+      !make_tmap_i8(&maps.b64, p.D, p.dim, p.nd_tok, 64) ||
+      !make_tmap_i8(&maps.b32, p.D, p.dim, p.nd_tok, 32) ||
+      !make_tmap_i8(&maps.b16, p.D, p.dim, p.nd_tok, 16))
+    return cudaErrorNotSupported;
+  return gal_launch<true>(P, maps, s);
 }
 
 }  // namespace fms

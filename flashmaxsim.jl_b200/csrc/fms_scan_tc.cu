@@ -860,6 +860,18 @@ bool make_tmap_16(CUtensorMap* m, const void* base, uint32_t fmt, int dim, int64
   return tc::make_map(m, base, fmt, dim, rows, box_rows);
 }
 
+bool make_tmap_i8(CUtensorMap* m, const void* base, int dim, int64_t rows, int box_rows) {
+  tc::EncodeTiledFn enc = tc::encode_fn();
+  if (!enc) return false;
+  cuuint64_t gdim[2] = {(cuuint64_t)dim, (cuuint64_t)rows};
+  cuuint64_t gstride[1] = {(cuuint64_t)dim};
+  cuuint32_t box[2] = {128u, (cuuint32_t)box_rows};
+  cuuint32_t estride[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), gdim, gstride, box, estride,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 int read_device_error(int reset) {
   int v = 0;
   cudaError_t e = cudaMemcpyFromSymbol(&v, g_tc_error, sizeof(int));
