@@ -71,6 +71,9 @@ SIGNATURES = {
     "fms_int8_topk_workspace_size": (_sz, [_i, _i64, _i]),
     "fms_int8_exhaustive_fwd": (_i, [_i, _i, _P, _P, _P, _P, _P, _P, _i, _i, _i, _i, _i64, _i,
                                      _P, _i, _P, _P, _i64, _P, _sz, _P]),
+    "fms_int8_exhaustive_float_workspace_size": (_sz, [_i, _i, _i, _i64, _i]),
+    "fms_int8_exhaustive_float_fwd": (_i, [_i, _P, _i, _P, _P, _P, _P, _i, _i, _i, _i, _i64, _i,
+                                           _P, _i, _P, _P, _i64, _P, _sz, _P]),
     "fms_topk_merge": (_i, [_P, _P, _i, _i, _i, _P, _P, _P]),
     "fms_candidates_finalize_neg": (_i, [_P, _i64, _i, _i, _d, _P, _P]),
     # multi-GPU (NCCL)

@@ -485,6 +485,33 @@ size_t fms_int8_topk_workspace_size(int nq, int64_t N, int k) {
   return ((size_t)N * (size_t)nq * 4 + 255) / 256 * 256 + topk_workspace_bytes(nq, N, k);
 }
 
+// The exhaustive scan + top-k for prepared parameters (quantised queries in
+// Qc / Qs, or float queries in Qf for the tensor-core prologue).
+static int exhaustive_run(Int8ScanParams& p, float* S, int k, float* topk_vals, int32_t* topk_ids,
+                          int64_t id_offset, void* workspace, size_t ws_bytes, cudaStream_t s) {
+  const int64_t N = p.N;
+  const int nq = (int)(N > 0 ? p.nunits / N : 0);
+  float* Sbuf = S;
+  char* ws = static_cast<char*>(workspace);
+  if (k > 0) {
+    size_t need = fms_int8_topk_workspace_size(nq, N, k);
+    if (!workspace || ws_bytes < need) return FMS_ERR_WORKSPACE;
+    if (!Sbuf) Sbuf = reinterpret_cast<float*>(ws);
+    ws += ((size_t)N * (size_t)nq * 4 + 255) / 256 * 256;
+  } else if (!S) {
+    return FMS_ERR_INVALID;
+  }
+  p.scores = Sbuf;
+  cudaError_t e = launch_int8_exhaustive_tc(p, s);
+  if (e == cudaErrorNotSupported && p.Qf == nullptr) e = launch_int8_scan(p, s);
+  if (e != cudaSuccess) return (int)e;
+  if (k > 0) {
+    e = launch_topk(Sbuf, N, nq, k, id_offset, ws, topk_vals, topk_ids, s);
+    if (e != cudaSuccess) return (int)e;
+  }
+  return FMS_OK;
+}
+
 int fms_int8_exhaustive_fwd(int qs_dtype, int ds_dtype, const int8_t* Qc, const void* Qs,
                             const int8_t* Gc, const void* Gs, const uint8_t* qmask,
                             const uint8_t* dmask, int dim, int Tq, int nq, int Td, int64_t N,
@@ -496,31 +523,61 @@ int fms_int8_exhaustive_fwd(int qs_dtype, int ds_dtype, const int8_t* Qc, const 
   if (k > 4096) return FMS_ERR_INVALID;
   if (k > 0 && (!topk_vals || !topk_ids)) return FMS_ERR_INVALID;
   if (N + id_offset >= (int64_t)INT32_MAX) return FMS_ERR_INVALID;
-  cudaStream_t s = (cudaStream_t)stream;
-  float* Sbuf = S;
-  char* ws = static_cast<char*>(workspace);
-  if (k > 0) {
-    size_t need = fms_int8_topk_workspace_size(nq, N, k);
-    if (!workspace || ws_bytes < need) return FMS_ERR_WORKSPACE;
-    if (!Sbuf) Sbuf = reinterpret_cast<float*>(ws);
-    ws += ((size_t)N * (size_t)nq * 4 + 255) / 256 * 256;
-  } else if (!S) {
-    return FMS_ERR_INVALID;
-  }
   Int8ScanParams p;
   memset(&p, 0, sizeof(p));
   p.Qc = Qc; p.Qs = Qs; p.Dc = Gc; p.Ds = Gs; p.qmask = qmask; p.dmask = dmask;
   p.qs_dtype = qs_dtype; p.ds_dtype = ds_dtype;
   p.dim = dim; p.Tq = Tq; p.Td = Td; p.exhaustive = 1; p.N = N; p.nunits = N * nq;
-  p.normalize = normalize; p.scores = Sbuf; p.args = nullptr;
-  cudaError_t e = launch_int8_exhaustive_tc(p, s);
-  if (e == cudaErrorNotSupported) e = launch_int8_scan(p, s);
+  p.normalize = normalize; p.args = nullptr;
+  return exhaustive_run(p, S, k, topk_vals, topk_ids, id_offset, workspace, ws_bytes,
+                        (cudaStream_t)stream);
+}
+
+static size_t al256(size_t x) { return (x + 255) / 256 * 256; }
+
+size_t fms_int8_exhaustive_float_workspace_size(int nq, int Tq, int dim, int64_t N, int k) {
+  if (nq < 0 || Tq < 0 || dim < 0 || N < 0 || k < 0) return 0;
+  const size_t ntok = (size_t)nq * (size_t)Tq;
+  return al256(k > 0 ? fms_int8_topk_workspace_size(nq, N, k) : 0) + al256(ntok * (size_t)dim) +
+         al256(ntok * 4);
+}
+
+int fms_int8_exhaustive_float_fwd(int q_dtype, const void* Q, int ds_dtype, const int8_t* Gc,
+                                  const void* Gs, const uint8_t* qmask, const uint8_t* dmask,
+                                  int dim, int Tq, int nq, int Td, int64_t N, int normalize,
+                                  float* S, int k, float* topk_vals, int32_t* topk_ids,
+                                  int64_t id_offset, void* workspace, size_t ws_bytes,
+                                  fms_stream_t stream) {
+  if (q_dtype != FMS_F32 && q_dtype != FMS_F16 && q_dtype != FMS_BF16) return FMS_ERR_DTYPE;
+  if (!scale_ok(ds_dtype)) return FMS_ERR_DTYPE;
+  if (dim < 0 || Tq < 0 || nq < 0 || Td < 0 || N < 0 || k < 0) return FMS_ERR_INVALID;
+  if (k > 4096) return FMS_ERR_INVALID;
+  if (k > 0 && (!topk_vals || !topk_ids)) return FMS_ERR_INVALID;
+  if (N + id_offset >= (int64_t)INT32_MAX) return FMS_ERR_INVALID;
+  const size_t need = fms_int8_exhaustive_float_workspace_size(nq, Tq, dim, N, k);
+  if (need > 0 && (!workspace || ws_bytes < need)) return FMS_ERR_WORKSPACE;
+  cudaStream_t s = (cudaStream_t)stream;
+  Int8ScanParams p;
+  memset(&p, 0, sizeof(p));
+  p.Dc = Gc; p.Ds = Gs; p.qmask = qmask; p.dmask = dmask;
+  p.qs_dtype = FMS_F32; p.ds_dtype = ds_dtype;
+  p.dim = dim; p.Tq = Tq; p.Td = Td; p.exhaustive = 1; p.N = N; p.nunits = N * nq;
+  p.normalize = normalize; p.args = nullptr;
+  p.Qf = Q; p.qf_dtype = q_dtype;
+  const size_t topk_part = al256(k > 0 ? fms_int8_topk_workspace_size(nq, N, k) : 0);
+  if (int8_exhaustive_tc_supported(p))
+    return exhaustive_run(p, S, k, topk_vals, topk_ids, id_offset, workspace, topk_part, s);
+  // shapes the tensor-core scan does not take: quantise into the workspace,
+  // then the scan of quantised queries
+  if (q_dtype == FMS_BF16) return FMS_ERR_DTYPE;  // the CUDA-core scan reads f32 / f16 scales
+  char* w = static_cast<char*>(workspace) + topk_part;
+  int8_t* qc = reinterpret_cast<int8_t*>(w);
+  void* qs = w + al256((size_t)nq * Tq * dim);
+  cudaError_t e = launch_quantize(q_dtype, Q, dim, (int64_t)nq * Tq, qc, qs, s);
   if (e != cudaSuccess) return (int)e;
-  if (k > 0) {
-    e = launch_topk(Sbuf, N, nq, k, id_offset, ws, topk_vals, topk_ids, s);
-    if (e != cudaSuccess) return (int)e;
-  }
-  return FMS_OK;
+  p.Qf = nullptr;
+  p.Qc = qc; p.Qs = qs; p.qs_dtype = q_dtype;
+  return exhaustive_run(p, S, k, topk_vals, topk_ids, id_offset, workspace, topk_part, s);
 }
 
 int fms_topk_merge(const float* vals, const int32_t* ids, int k, int nq, int nshard,

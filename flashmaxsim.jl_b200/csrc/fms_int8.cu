@@ -6,48 +6,23 @@
 #include "fms_common.cuh"
 #include "fms_internal.h"
 #include "fms_int8.cuh"
+#include "fms_quant.cuh"
 
 namespace fms {
 
 // ------------------------------------------------------------------ quantize
 
-// quantize_int8_symmetric (quant.jl:42-49), one warp per token.  Each op is
-// rounded to T as Julia's Float16/BFloat16 arithmetic does.
+// quantize_int8_symmetric (quant.jl:42-49), one warp per token (fms_quant.cuh).
 template <typename T>
 __global__ void quantize_kernel(const T* __restrict__ x, int dim, int64_t ntok,
                                 int8_t* __restrict__ codes, T* __restrict__ scales) {
-  using A = typename Tr<T>::Acc;
   const int lane = threadIdx.x & 31;
   const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  // T(1f-8) and floatmin(T) (quant.jl:21-22)
-  const A eps = Tr<T>::to(Tr<T>::from((A)1e-8f));
-  const A fmin = Tr<T>::floatmin();
   for (int64_t t = w; t < ntok; t += nw) {
-    const T* xt = x + t * dim;
-    A am = (A)0;
-    bool nan = false;
-    for (int k = lane; k < dim; k += 32) {
-      A a = fabs(Tr<T>::to(xt[k]));
-      if (a != a) nan = true;
-      am = a > am ? a : am;
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-      A o = __shfl_xor_sync(0xffffffffu, am, off);
-      am = o > am ? o : am;
-    }
-    nan = __any_sync(0xffffffffu, nan);
-    if (nan) am = (A)NAN;
-    A raw = Tr<T>::to(Tr<T>::from(((am != am || am > eps) ? am : eps) / (A)127));
-    A sc = (raw != raw || raw > fmin) ? raw : fmin;
+    int8_t* ct = codes + t * dim;
+    const auto sc = quantize_token<T>(x + t * dim, dim, lane, [&](int k, int8_t c) { ct[k] = c; });
     if (lane == 0) scales[t] = Tr<T>::from(sc);
-    for (int k = lane; k < dim; k += 32) {
-      A v = Tr<T>::to(Tr<T>::from(Tr<T>::to(xt[k]) / sc));
-      v = v < (A)-127 ? (A)-127 : (v > (A)127 ? (A)127 : v);
-      if (v != v) v = (A)0;  // the reference throws InexactError on NaN
-      codes[t * dim + k] = (int8_t)rint(v);
-    }
   }
 }
 

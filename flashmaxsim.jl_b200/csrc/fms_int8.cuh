@@ -20,6 +20,8 @@ struct Int8ScanParams {
   int normalize;
   float* scores;          // paired (B,), exhaustive (N, nq)
   int32_t* args;          // (Tq, units) or NULL
+  const void* Qf;         // exhaustive tensor-core scan only: float queries quantised
+  int qf_dtype;           //   in its prologue instead of Qc / Qs (NULL = use Qc / Qs)
 };
 
 cudaError_t launch_quantize(int dtype, const void* x, int dim, int64_t ntok, int8_t* codes,

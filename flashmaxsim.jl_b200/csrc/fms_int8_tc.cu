@@ -42,6 +42,7 @@
 #include "fms_common.cuh"
 #include "fms_internal.h"
 #include "fms_int8.cuh"
+#include "fms_quant.cuh"
 #include "fms_tc_ptx.cuh"
 
 namespace fms {
@@ -71,6 +72,8 @@ constexpr int BIAS_BYTES = 512;           // two 8-row x 32-byte tiles (K = 16 f
 
 struct Params {
   const void* Qs;         // query scales (nq_total, Tq): f32 or f16
+  const void* Qf;         // float queries (nq_total, Tq, dim) quantised in the prologue, or NULL
+  int qf_dtype;           // FMS_F32 / FMS_F16 / FMS_BF16 of Qf
   const void* Gs;         // document scales (N, Td): f32 or f16
   const uint8_t* qmask;   // (nq_total, Tq) or NULL
   const uint8_t* dmask;   // (N, Td) or NULL
@@ -202,7 +205,7 @@ i8_exhaustive_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
     ptx::fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
-    ptx::prefetch_tmap(&tmQ);
+    if (P.Qf == nullptr) ptx::prefetch_tmap(&tmQ);
     ptx::prefetch_tmap(&tmG);
   }
   if (warp == 2) {
@@ -221,14 +224,43 @@ i8_exhaustive_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
     for (int qi = warp - 2; qi < P.MT * 4; qi += NEPI) {
       bool tv = false;
       float qsv = 0.f;
-      if (qi < P.nq && lane < P.Tq) {
+      const bool real = qi < P.nq && lane < P.Tq;
+      if (real) {
         const int64_t qr = (int64_t)(P.q0 + qi) * P.Tq + lane;
         tv = P.qmask == nullptr || P.qmask[qr] != 0;
-        qsv = ld_scale(P.Qs, P.qs_f16, qr);
+        if (P.Qf == nullptr) qsv = ld_scale(P.Qs, P.qs_f16, qr);
       }
-      qs_s[qi][lane] = qsv;
+      if (P.Qf == nullptr || !real) qs_s[qi][lane] = qsv;  // fused: written by the quantiser
       const uint32_t vw = __ballot_sync(0xffffffffu, tv);
       if (lane == 0) qv_s[qi] = vw;
+    }
+    if (P.Qf != nullptr) {
+      // Fused query quantisation (quant.jl:42-49, as the reference quantises on
+      // every call, quant.jl:159): one warp per query token writes its codes
+      // straight into the resident A tiles in the 128-byte swizzled layout the
+      // MMA reads (16-byte chunk c of row r stored at chunk c ^ (r & 7)), and
+      // its scale into qs_s.
+      const int ntok = P.nq * P.Tq;
+      for (int tk = warp - 2; tk < ntok; tk += NEPI) {
+        const int qi = tk / P.Tq, t = tk - qi * P.Tq;
+        const int row = (qi & 3) * 32 + t;
+        unsigned char* tile0 = aregion + (qi >> 2) * P.KB * A_TILE + row * ROWB;
+        auto emit = [&](int k, int8_t c) {
+          const int kb = k >> 7, b = k & 127;
+          tile0[kb * A_TILE + ((((b >> 4) ^ (row & 7)) << 4) | (b & 15))] = (unsigned char)c;
+        };
+        const int64_t off = ((int64_t)(P.q0 + qi) * P.Tq + t) * P.KB * 128;
+        float sc;
+        if (P.qf_dtype == FMS_F16)
+          sc = quantize_token<__half>(static_cast<const __half*>(P.Qf) + off, P.KB * 128, lane, emit);
+        else if (P.qf_dtype == FMS_BF16)
+          sc = quantize_token<__nv_bfloat16>(static_cast<const __nv_bfloat16*>(P.Qf) + off, P.KB * 128,
+                                             lane, emit);
+        else
+          sc = quantize_token<float>(static_cast<const float*>(P.Qf) + off, P.KB * 128, lane, emit);
+        if (lane == 0) qs_s[qi][t] = sc;
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> MMA reads
     }
   }
   if (warp == 1) ptx::tmem_alloc(&tmem_base_s, 512);
@@ -242,12 +274,16 @@ i8_exhaustive_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      // resident queries: query qi -> rows [32 (qi % 4), +32) of M tile qi / 4
-      ptx::mbar_expect_tx(&afull_bar, (uint32_t)(P.nq * P.KB * 32 * ROWB));
-      for (int qi = 0; qi < P.nq; ++qi)
-        for (int kb = 0; kb < P.KB; ++kb)
-          ptx::tma_load_2d(aregion + ((qi >> 2) * P.KB + kb) * A_TILE + (qi & 3) * 32 * ROWB, &tmQ,
-                           kb * 128, (P.q0 + qi) * P.Tq, &afull_bar);
+      if (P.Qf != nullptr) {
+        ptx::mbar_arrive(&afull_bar);  // the prologue wrote the tiles before the block barrier
+      } else {
+        // resident queries: query qi -> rows [32 (qi % 4), +32) of M tile qi / 4
+        ptx::mbar_expect_tx(&afull_bar, (uint32_t)(P.nq * P.KB * 32 * ROWB));
+        for (int qi = 0; qi < P.nq; ++qi)
+          for (int kb = 0; kb < P.KB; ++kb)
+            ptx::tma_load_2d(aregion + ((qi >> 2) * P.KB + kb) * A_TILE + (qi & 3) * 32 * ROWB, &tmQ,
+                             kb * 128, (P.q0 + qi) * P.Tq, &afull_bar);
+      }
     }
     __syncwarp();
     for (int64_t i = 0; i < my_st; ++i) {
@@ -493,6 +529,7 @@ cudaError_t launch_int8_exhaustive_tc(const Int8ScanParams& p, cudaStream_t s) {
   const int nq_total = (int)(p.nunits / p.N);
   Params P;
   P.Qs = p.Qs; P.Gs = p.Ds; P.qmask = p.qmask; P.dmask = p.dmask; P.S = p.scores;
+  P.Qf = p.Qf; P.qf_dtype = p.qf_dtype;
   P.N = p.N;
   P.qs_f16 = p.qs_dtype == FMS_F16; P.ds_f16 = p.ds_dtype == FMS_F16;
   P.Tq = p.Tq; P.Td = p.Td;
@@ -506,7 +543,9 @@ cudaError_t launch_int8_exhaustive_tc(const Int8ScanParams& p, cudaStream_t s) {
   P.nstages = (p.N + P.dps - 1) / P.dps;
   P.normalize = p.normalize;
   CUtensorMap tq, tg;
-  if (!make_map_i8(&tq, p.Qc, p.dim, (int64_t)nq_total * p.Tq, 32)) return cudaErrorNotSupported;
+  memset(&tq, 0, sizeof(tq));  // unused when the queries are quantised in the prologue
+  if (p.Qf == nullptr && !make_map_i8(&tq, p.Qc, p.dim, (int64_t)nq_total * p.Tq, 32))
+    return cudaErrorNotSupported;
   if (!make_map_i8(&tg, p.Dc, p.dim, p.N * (int64_t)p.Td, P.Tdp)) return cudaErrorNotSupported;
   const int mt_max = max_mtiles(P.KB);
   const int qpp = 4 * mt_max;  // queries per pass over the index

@@ -450,7 +450,10 @@ def int8_exhaustive_forward(Q, index: Int8Index, qmask=None, dmask=None, normali
     Returns S (nq,N) when topk is None, else (vals (nq,k), ids (nq,k) 1-based,
     plus id_offset) and S too when return_scores=True."""
     require_int8_index(index)
-    QQ = quantized if quantized is not None else quantize_int8_symmetric(Q)
+    if quantized is None:
+        return _int8_exhaustive_float(Q, index, qmask, dmask, normalize, topk, id_offset,
+                                      return_scores)
+    QQ = quantized
     nq, Tq, dim = QQ.codes.shape
     N, Td = index.codes.shape[0], index.codes.shape[1]
     if index.codes.shape[2] != dim:
@@ -470,6 +473,40 @@ def int8_exhaustive_forward(Q, index: Int8Index, qmask=None, dmask=None, normali
         ws = torch.empty(nb, dtype=torch.uint8, device=dev)
     _run("fms_int8_exhaustive_fwd", dev, _scale_code(QQ.scales), _scale_code(index.scales),
          _lib.ptr(QQ.codes), _lib.ptr(QQ.scales), _lib.ptr(index.codes.contiguous()),
+         _lib.ptr(index.scales.contiguous()), _lib.ptr(qm), _lib.ptr(dm), dim, Tq, nq, Td, N,
+         int(normalize), _lib.ptr(S), k, _lib.ptr(vals), _lib.ptr(ids), int(id_offset),
+         _lib.ptr(ws), nb)
+    if k == 0:
+        return S
+    return (vals, ids, S) if return_scores else (vals, ids)
+
+
+def _int8_exhaustive_float(Q, index, qmask, dmask, normalize, topk, id_offset, return_scores):
+    """fms_int8_exhaustive_float_fwd: the queries are quantised inside the scan
+    (quant.jl:159 quantises them on every call) -- one launch, no quantised copy."""
+    if Q.dim() != 3:
+        raise DimensionMismatch("INT8 search expects (nq, Tq, dim) queries")
+    if Q.dtype not in (torch.float32, torch.float16, torch.bfloat16):
+        raise ArgumentError(f"INT8 search: unsupported query dtype {Q.dtype}")
+    nq, Tq, dim = Q.shape
+    N, Td = index.codes.shape[0], index.codes.shape[1]
+    if index.codes.shape[2] != dim:
+        raise DimensionMismatch("feature dim")
+    dev = _device_of(Q, index.codes, index.scales, qmask, dmask)
+    Q = Q.contiguous()
+    qm = _mask(qmask, (nq, Tq), "qmask")
+    dm = _mask(dmask, (N, Td), "dmask")
+    k = 0 if topk is None else int(topk)
+    want_S = topk is None or bool(return_scores)
+    S = torch.empty((nq, N), dtype=torch.float32, device=dev) if want_S else None
+    vals = ids = None
+    if k > 0:
+        vals = torch.empty((nq, k), dtype=torch.float32, device=dev)
+        ids = torch.empty((nq, k), dtype=torch.int32, device=dev)
+    nb = _lib.lib().fms_int8_exhaustive_float_workspace_size(nq, Tq, dim, N, k)
+    ws = torch.empty(max(nb, 1), dtype=torch.uint8, device=dev)
+    _run("fms_int8_exhaustive_float_fwd", dev, _lib.DTYPE_CODE[Q.dtype], _lib.ptr(Q),
+         _scale_code(index.scales), _lib.ptr(index.codes.contiguous()),
          _lib.ptr(index.scales.contiguous()), _lib.ptr(qm), _lib.ptr(dm), dim, Tq, nq, Td, N,
          int(normalize), _lib.ptr(S), k, _lib.ptr(vals), _lib.ptr(ids), int(id_offset),
          _lib.ptr(ws), nb)

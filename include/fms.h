@@ -249,6 +249,20 @@ int fms_int8_exhaustive_fwd(int qs_dtype, int ds_dtype, const int8_t* Qc, const 
                             int32_t* topk_ids, int64_t id_offset, void* workspace,
                             size_t ws_bytes, fms_stream_t stream);
 
+/* The same search for float queries Q (dim,Tq,nq) in q_dtype (FMS_F32, FMS_F16 or
+   FMS_BF16): quantize_int8_symmetric (quant.jl:42-49, every op in q_dtype) runs
+   inside the tensor-core scan's prologue, as the reference quantises queries on
+   every call (quant.jl:159), so no quantised copy of the queries is written;
+   shapes the tensor-core scan does not take quantise into the workspace first
+   (f32 / f16 queries).  Workspace: fms_int8_exhaustive_float_workspace_size. */
+size_t fms_int8_exhaustive_float_workspace_size(int nq, int Tq, int dim, int64_t N, int k);
+int fms_int8_exhaustive_float_fwd(int q_dtype, const void* Q, int ds_dtype, const int8_t* Gc,
+                                  const void* Gs, const uint8_t* qmask, const uint8_t* dmask,
+                                  int dim, int Tq, int nq, int Td, int64_t N, int normalize,
+                                  float* S, int k, float* topk_vals, int32_t* topk_ids,
+                                  int64_t id_offset, void* workspace, size_t ws_bytes,
+                                  fms_stream_t stream);
+
 /* Merge per-shard top-k lists: vals/ids (k,nq,nshard) -> out (k,nq), same order
    rule.  Used after an all-gather of shard results. */
 int fms_topk_merge(const float* vals, const int32_t* ids, int k, int nq, int nshard,

@@ -102,3 +102,27 @@ def test_exhaustive_tc_topk_matches_oracle_ranking(fms, oracle):
     if not same.all():
         r, c = np.nonzero(~same)
         assert np.allclose(So[r, ids.cpu().numpy()[r, c] - 1], vo[r, c], rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("qdt", [torch.float16, torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("nq,Tq,Td,dim,N", [(40, 32, 128, 128, 901), (6, 9, 100, 256, 333)])
+def test_fused_query_quantisation_matches(fms, oracle, qdt, nq, Tq, Td, dim, N):
+    """Float queries quantised inside the scan's prologue (one launch) give the
+    same scores and top-k, bit for bit, as quantize_int8_symmetric followed by
+    the scan of the quantised queries, over several query passes, with masks."""
+    rng = seeded(70 + nq + dim)
+    Q = torch.from_numpy(l2cols(rng.standard_normal((nq, Tq, dim)))).to(qdt).cuda()
+    G = torch.from_numpy(l2cols(rng.standard_normal((N, Td, dim)))).cuda()
+    index = fms.quantize_int8_symmetric(G)
+    qm = torch.from_numpy(rng.random((nq, Tq)) > 0.1).cuda()
+    dm = torch.from_numpy(rng.random((N, Td)) > 0.2).cuda()
+    v, i, S = fms.int8_exhaustive_forward(Q, index, qm, dm, topk=17, return_scores=True)
+    QQ = fms.quantize_int8_symmetric(Q)
+    if qdt == torch.bfloat16:   # the separate path reads f32 / f16 scales
+        QQ = fms.Int8Index(QQ.codes, QQ.scales.float())
+    v2, i2, S2 = fms.int8_exhaustive_forward(None, index, qm, dm, topk=17, return_scores=True,
+                                             quantized=QQ)
+    assert torch.equal(S, S2) and torch.equal(v, v2) and torch.equal(i, i2)
+    So = oracle.int8_exhaustive(QQ.codes, QQ.scales.float(), index.codes, index.scales,
+                                qm.cpu(), dm.cpu())
+    assert_scores(S.cpu(), So, 1e-5)
