@@ -107,25 +107,69 @@ def doc_tokens(idxs, lens, world, rank):
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    """SM clocks and throttle reasons sampled while the timed region runs.
 
+    A thread polls NVML (read-only queries: current and maximum SM clock, the
+    active clock-event reasons) every 2 ms from start() to stop(), so that even
+    a timed region of a few milliseconds carries samples; nvidia-smi at its
+    shortest interval is the fallback when NVML cannot be opened."""
+
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, dev_index):
-        self.path = tempfile.mktemp(suffix=".csv")
-        self.proc = None
         self.uuid = None
         try:
             self.uuid = "GPU-" + str(torch.cuda.get_device_properties(dev_index).uuid)
         except Exception:
             pass
+        self.dev_index = dev_index
+        self.samples = []   # (sm MHz, max sm MHz, set of reasons)
+        self.thread = None
+        self.proc = None
+
+    def _nvml_handle(self):
+        import pynvml as N
+        N.nvmlInit()
+        if self.uuid:
+            return N, N.nvmlDeviceGetHandleByUUID(self.uuid)
+        return N, N.nvmlDeviceGetHandleByIndex(self.dev_index)
 
     def start(self):
+        import threading
+        try:
+            N, h = self._nvml_handle()
+            bits = {"hw_slowdown": N.nvmlClocksEventReasonHwSlowdown,
+                    "hw_thermal_slowdown": N.nvmlClocksEventReasonHwThermalSlowdown,
+                    "sw_thermal_slowdown": N.nvmlClocksEventReasonSwThermalSlowdown,
+                    "sw_power_cap": N.nvmlClocksEventReasonSwPowerCap}
+            smax = N.nvmlDeviceGetMaxClockInfo(h, N.NVML_CLOCK_SM)
+        except Exception:
+            self._start_smi()
+            return
+        self.stop_flag = threading.Event()
+
+        def poll():
+            while not self.stop_flag.is_set():
+                try:
+                    sm = N.nvmlDeviceGetClockInfo(h, N.NVML_CLOCK_SM)
+                    r = N.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    self.samples.append((float(sm), float(smax),
+                                         {k for k, m in bits.items() if r & m}))
+                except Exception:
+                    pass
+                self.stop_flag.wait(0.002)
+
+        self.thread = threading.Thread(target=poll, daemon=True)
+        self.thread.start()
+
+    def _start_smi(self):
+        self.path = tempfile.mktemp(suffix=".csv")
         try:
             cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                   "-lms", "200"]
+                   "-lms", "100"]
             if self.uuid:
                 cmd += ["-i", self.uuid]
             self.fh = open(self.path, "w")
@@ -134,32 +178,36 @@ class ClockSampler:
             self.proc = None
 
     def stop(self):
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
-        self.fh.close()
-        sm, smax, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in Path(self.path).read_text().splitlines():
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
+        if self.thread is not None:
+            self.stop_flag.set()
+            self.thread.join(timeout=5)
+            src = "nvml (2 ms)"
+        elif self.proc is not None:
+            self.proc.terminate()
             try:
-                sm.append(float(parts[1]))
-                smax.append(float(parts[2]))
-            except ValueError:
-                continue
-            for nm, v in zip(names, parts[5:9]):
-                if v.lower() == "active":
-                    reasons.add(nm)
-        os.unlink(self.path)
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.fh.close()
+            for line in Path(self.path).read_text().splitlines():
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm, smax = float(parts[1]), float(parts[2])
+                except ValueError:
+                    continue
+                self.samples.append((sm, smax, {nm for nm, v in zip(self.NAMES, parts[5:9])
+                                                if v.lower() == "active"}))
+            os.unlink(self.path)
+            src = "nvidia-smi (100 ms)"
+        else:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [x[0] for x in self.samples]
+        reasons = set().union(*[x[2] for x in self.samples]) if self.samples else set()
         return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": max(smax) if smax else None,
-                "samples": len(sm), "reasons": sorted(reasons)}
+                "sm_max_mhz": max(x[1] for x in self.samples) if sm else None,
+                "samples": len(sm), "source": src, "reasons": sorted(reasons)}
 
 
 def arm_config(world, total_tok):
@@ -478,7 +526,6 @@ def main():
         dist.barrier()
     clocks = ClockSampler(local)
     clocks.start()
-    time.sleep(0.3)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     if world > 1:

@@ -456,6 +456,82 @@ __device__ __forceinline__ bool unit_row(const BwdParams& b, int64_t u, int64_t 
 // Warp per query-token row: dQ gather (+ dD float32 atomics when ATOMIC).
 constexpr int VEC_UNROLL = 2;  // rows in flight per warp
 
+// Rows (documents or sources) in flight per warp: four for rows of up to 96 vectors, two for
+// wider ones (register budget)
+template <int NV> struct RowsInFlight { static constexpr int n = NV <= 3 ? 4 : 2; };
+
+// In-batch dQ (no atomics): the tape entries and deltas of 32 documents are
+// loaded at once, one per lane, and broadcast; RowsInFlight rows are in flight
+// at a time.  Documents are still summed in ascending order with one
+// fused multiply-add per element, so the result is the same as the generic
+// kernel's.
+
+template <typename T, int NV>
+__device__ __forceinline__ void inb_gather_row(const BwdParams& b, int64_t r, int lane) {
+  constexpr int E = V16<T>::E;
+  constexpr int GB_ROWS = RowsInFlight<NV>::n;
+  const ScanParams& p = b.g;
+  const uint4* D = static_cast<const uint4*>(p.D);
+  uint4* dQ = static_cast<uint4*>(b.dQ);
+  const int nvec = p.dim / E;
+  const int64_t qi = r / p.Tq;
+  const int t = (int)(r - qi * p.Tq);
+  const bool live = p.qmask == nullptr || p.qmask[qi * p.Tq + t];
+  float acc[NV][E];
+#pragma unroll
+  for (int k = 0; k < NV; ++k)
+#pragma unroll
+    for (int e = 0; e < E; ++e) acc[k][e] = 0.f;
+  for (int64_t j0 = 0; live && j0 < p.Bd; j0 += 32) {
+    // lane d: document j0 + d
+    int my_a = 0;
+    float my_dl = 0.f;
+    if (j0 + lane < p.Bd) {
+      const int64_t u = qi * p.Bd + j0 + lane;
+      my_a = p.args[u * p.Tq + t];
+      if (my_a >= 1 && my_a <= p.Td) my_dl = unit_delta<T>(b, u, (int)qi);
+      else my_a = 0;
+    }
+    const int nd = (int)min((int64_t)32, p.Bd - j0);
+    for (int d0 = 0; d0 < nd; d0 += GB_ROWS) {
+      int a[GB_ROWS];
+      float dl[GB_ROWS];
+      uint4 dv[GB_ROWS][NV];
+#pragma unroll
+      for (int q = 0; q < GB_ROWS; ++q) {
+        a[q] = __shfl_sync(0xffffffffu, my_a, (d0 + q) & 31);
+        dl[q] = __shfl_sync(0xffffffffu, my_dl, (d0 + q) & 31);
+        if (d0 + q >= nd) a[q] = 0;
+        const int64_t drow = (j0 + d0 + q) * p.Td + a[q] - 1;
+#pragma unroll
+        for (int k = 0; k < NV; ++k) {
+          const int v = lane + 32 * k;
+          if (a[q] && v < nvec) dv[q][k] = D[drow * nvec + v];
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < GB_ROWS; ++q) {
+        if (!a[q]) continue;
+#pragma unroll
+        for (int k = 0; k < NV; ++k) {
+          const int v = lane + 32 * k;
+          if (v < nvec) {
+            float x[E];
+            unpack(dv[q][k], x, (T*)nullptr);
+#pragma unroll
+            for (int e = 0; e < E; ++e) acc[k][e] += dl[q] * x[e];
+          }
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int v = lane + 32 * k;
+    if (v < nvec) dQ[r * nvec + v] = pack(acc[k], (T*)nullptr);
+  }
+}
+
 template <typename T, bool ATOMIC, int NV, bool INB>
 __global__ void __launch_bounds__(256, 2) bwd_gather_vec_kernel(BwdParams b, float* dD_acc) {
   constexpr int E = V16<T>::E;
@@ -467,72 +543,78 @@ __global__ void __launch_bounds__(256, 2) bwd_gather_vec_kernel(BwdParams b, flo
   const uint4* D = static_cast<const uint4*>(p.D);
   uint4* dQ = static_cast<uint4*>(b.dQ);
   const int nvec = p.dim / E;  // 16-byte vectors per row
-  for (int64_t r = warp; r < b.nq_rows; r += nwarps) {
-    int64_t u0, cnt;
-    int t;
-    units_of_row(p, r, u0, cnt, t);
-    const int64_t qi = INB ? r / p.Tq : 0;
-    float acc[NV][E];
-    float qv[NV][E];
+  if constexpr (INB && !ATOMIC) {
+    for (int64_t r = warp; r < b.nq_rows; r += nwarps) inb_gather_row<T, NV>(b, r, lane);
+  } else {
+    for (int64_t r = warp; r < b.nq_rows; r += nwarps) {
+      int64_t u0, cnt;
+      int t;
+      units_of_row(p, r, u0, cnt, t);
+      const int64_t qi = INB ? r / p.Tq : 0;
+      float acc[NV][E];
+      float qv[NV][E];
 #pragma unroll
-    for (int k = 0; k < NV; ++k) {
-      const int v = lane + 32 * k;
+      for (int k = 0; k < NV; ++k) {
+        const int v = lane + 32 * k;
 #pragma unroll
-      for (int e = 0; e < E; ++e) { acc[k][e] = 0.f; qv[k][e] = 0.f; }
-      if (ATOMIC && v < nvec) unpack(Q[r * nvec + v], qv[k], (T*)nullptr);
-    }
-    for (int64_t i0 = 0; i0 < cnt; i0 += VEC_UNROLL) {
-      int64_t drow[VEC_UNROLL];
-      float dl[VEC_UNROLL];
-      bool ok[VEC_UNROLL];
-#pragma unroll
-      for (int q = 0; q < VEC_UNROLL; ++q) {
-        ok[q] = i0 + q < cnt && unit_row<T, INB>(b, u0 + i0 + q, qi, i0 + q, t, drow[q], dl[q]);
+        for (int e = 0; e < E; ++e) { acc[k][e] = 0.f; qv[k][e] = 0.f; }
+        if (ATOMIC && v < nvec) unpack(Q[r * nvec + v], qv[k], (T*)nullptr);
       }
-      uint4 dv[VEC_UNROLL][NV];
+      for (int64_t i0 = 0; i0 < cnt; i0 += VEC_UNROLL) {
+        int64_t drow[VEC_UNROLL];
+        float dl[VEC_UNROLL];
+        bool ok[VEC_UNROLL];
 #pragma unroll
-      for (int q = 0; q < VEC_UNROLL; ++q)
-#pragma unroll
-        for (int k = 0; k < NV; ++k) {
-          const int v = lane + 32 * k;
-          if (ok[q] && v < nvec) dv[q][k] = D[drow[q] * nvec + v];
+        for (int q = 0; q < VEC_UNROLL; ++q) {
+          ok[q] = i0 + q < cnt && unit_row<T, INB>(b, u0 + i0 + q, qi, i0 + q, t, drow[q], dl[q]);
         }
+        uint4 dv[VEC_UNROLL][NV];
 #pragma unroll
-      for (int q = 0; q < VEC_UNROLL; ++q) {
-        if (!ok[q]) continue;
+        for (int q = 0; q < VEC_UNROLL; ++q)
 #pragma unroll
-        for (int k = 0; k < NV; ++k) {
-          const int v = lane + 32 * k;
-          if (v < nvec) {
-            float x[E];
-            unpack(dv[q][k], x, (T*)nullptr);
+          for (int k = 0; k < NV; ++k) {
+            const int v = lane + 32 * k;
+            if (ok[q] && v < nvec) dv[q][k] = D[drow[q] * nvec + v];
+          }
 #pragma unroll
-            for (int e = 0; e < E; ++e) acc[k][e] += dl[q] * x[e];
-            if (ATOMIC) {
-              float* dst = dD_acc + (drow[q] * nvec + v) * E;
+        for (int q = 0; q < VEC_UNROLL; ++q) {
+          if (!ok[q]) continue;
 #pragma unroll
-              for (int e = 0; e < E; e += 4)
-                atomicAdd(reinterpret_cast<float4*>(dst + e),
-                          make_float4(dl[q] * qv[k][e], dl[q] * qv[k][e + 1], dl[q] * qv[k][e + 2],
-                                      dl[q] * qv[k][e + 3]));
+          for (int k = 0; k < NV; ++k) {
+            const int v = lane + 32 * k;
+            if (v < nvec) {
+              float x[E];
+              unpack(dv[q][k], x, (T*)nullptr);
+#pragma unroll
+              for (int e = 0; e < E; ++e) acc[k][e] += dl[q] * x[e];
+              if (ATOMIC) {
+                float* dst = dD_acc + (drow[q] * nvec + v) * E;
+#pragma unroll
+                for (int e = 0; e < E; e += 4)
+                  atomicAdd(reinterpret_cast<float4*>(dst + e),
+                            make_float4(dl[q] * qv[k][e], dl[q] * qv[k][e + 1], dl[q] * qv[k][e + 2],
+                                        dl[q] * qv[k][e + 3]));
+              }
             }
           }
         }
       }
-    }
 #pragma unroll
-    for (int k = 0; k < NV; ++k) {
-      const int v = lane + 32 * k;
-      if (v < nvec) dQ[r * nvec + v] = pack(acc[k], (T*)nullptr);
+      for (int k = 0; k < NV; ++k) {
+        const int v = lane + 32 * k;
+        if (v < nvec) dQ[r * nvec + v] = pack(acc[k], (T*)nullptr);
+      }
     }
   }
 }
 
 // Warp per destination document token: sources summed in ascending id order.
+
 template <typename T, int NV, bool INB>
 __global__ void __launch_bounds__(SC_WARPS * 32, 2)
 csr_scatter_vec_kernel(BwdParams b, const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col_idx) {
   constexpr int E = V16<T>::E;
+  constexpr int SC_ROWS = RowsInFlight<NV>::n;
   __shared__ int32_t seg_s[SC_WARPS][SC_SEG];
   const ScanParams& p = b.g;
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
@@ -560,48 +642,55 @@ csr_scatter_vec_kernel(BwdParams b, const int32_t* __restrict__ row_ptr, const i
     for (int k = 0; k < NV; ++k)
 #pragma unroll
       for (int e = 0; e < E; ++e) acc[k][e] = 0.f;
-    for (int i0 = 0; i0 < n; i0 += VEC_UNROLL) {
-      int64_t qrow[VEC_UNROLL];
-      float dl[VEC_UNROLL];
-#pragma unroll
-      for (int q = 0; q < VEC_UNROLL; ++q) {
-        qrow[q] = -1;
-        dl[q] = 0.f;
-        if (i0 + q < n) {
-          // source ids are int32 (the CSR stores them so): 32-bit division
-          const uint32_t s = (uint32_t)(ranked ? seg[i0 + q] : col_idx[a0 + i0 + q]);
-          const uint32_t u = s / (uint32_t)p.Tq;
-          const int t = (int)(s - u * (uint32_t)p.Tq);
-          if constexpr (INB) {
-            const int64_t qi = u / (uint32_t)p.Bd;
-            qrow[q] = qi * p.Tq + t;
-            dl[q] = unit_delta<T>(b, u, (int)qi);
-          } else {
-            const Unit U = decode_unit(p, u);
-            qrow[q] = U.q0 + t;
-            dl[q] = unit_delta<T>(b, u, U.qidx);
-          }
+    for (int i0 = 0; i0 < n; i0 += 32) {
+      // lane l decodes source i0 + l (its query row and delta) once; the
+      // rows are then broadcast and summed in ascending order, SC_ROWS rows
+      // in flight
+      int64_t my_row = -1;
+      float my_dl = 0.f;
+      if (i0 + lane < n) {
+        // source ids are int32 (the CSR stores them so): 32-bit division
+        const uint32_t s = (uint32_t)(ranked ? seg[i0 + lane] : col_idx[a0 + i0 + lane]);
+        const uint32_t u = s / (uint32_t)p.Tq;
+        const int t = (int)(s - u * (uint32_t)p.Tq);
+        if constexpr (INB) {
+          const int64_t qi = u / (uint32_t)p.Bd;
+          my_row = qi * p.Tq + t;
+          my_dl = unit_delta<T>(b, u, (int)qi);
+        } else {
+          const Unit U = decode_unit(p, u);
+          my_row = U.q0 + t;
+          my_dl = unit_delta<T>(b, u, U.qidx);
         }
       }
-      uint4 qv[VEC_UNROLL][NV];
+      const int ns = min(32, n - i0);
+      for (int c0 = 0; c0 < ns; c0 += SC_ROWS) {
+        int64_t qrow[SC_ROWS];
+        float dl[SC_ROWS];
+        uint4 qv[SC_ROWS][NV];
 #pragma unroll
-      for (int q = 0; q < VEC_UNROLL; ++q)
+        for (int q = 0; q < SC_ROWS; ++q) {
+          qrow[q] = __shfl_sync(0xffffffffu, my_row, (c0 + q) & 31);
+          dl[q] = __shfl_sync(0xffffffffu, my_dl, (c0 + q) & 31);
+          if (c0 + q >= ns) qrow[q] = -1;
 #pragma unroll
-        for (int k = 0; k < NV; ++k) {
-          const int v = lane + 32 * k;
-          if (qrow[q] >= 0 && v < nvec) qv[q][k] = Q[qrow[q] * nvec + v];
+          for (int k = 0; k < NV; ++k) {
+            const int v = lane + 32 * k;
+            if (qrow[q] >= 0 && v < nvec) qv[q][k] = Q[qrow[q] * nvec + v];
+          }
         }
 #pragma unroll
-      for (int q = 0; q < VEC_UNROLL; ++q) {
-        if (qrow[q] < 0) continue;
+        for (int q = 0; q < SC_ROWS; ++q) {
+          if (qrow[q] < 0) continue;
 #pragma unroll
-        for (int k = 0; k < NV; ++k) {
-          const int v = lane + 32 * k;
-          if (v < nvec) {
-            float x[E];
-            unpack(qv[q][k], x, (T*)nullptr);
+          for (int k = 0; k < NV; ++k) {
+            const int v = lane + 32 * k;
+            if (v < nvec) {
+              float x[E];
+              unpack(qv[q][k], x, (T*)nullptr);
 #pragma unroll
-            for (int e = 0; e < E; ++e) acc[k][e] += dl[q] * x[e];
+              for (int e = 0; e < E; ++e) acc[k][e] += dl[q] * x[e];
+            }
           }
         }
       }
