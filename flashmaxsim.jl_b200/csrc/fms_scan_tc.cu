@@ -31,9 +31,14 @@
 //           boxes, stopping at the last valid token, so masked padding is not
 //           read) into an S-stage ring, with the query tile either resident
 //           (re-loaded only when the unit's query changes) or carried per stage;
-//   warp 1  MMA issuer (one elected lane): 4 K=16 MMAs per K block into one of
+//   warp 1 (+ warps 7, 8)  MMA issuers, one per query tile (one elected lane
+//           each): 4 K=16 MMAs per K block into the tile's columns of one of
 //           NACC TMEM accumulator buffers, tcgen05.commit to the ring slot and,
-//           after the chunk's last K block, to the accumulator barrier;
+//           after the chunk's last K block, to the accumulator barrier.  A single
+//           thread that waits on a barrier between MMA groups leaves the tensor
+//           pipe idle while it waits (a 128x128x16 MMA lasts 64 cycles, about
+//           what one completed-barrier check costs the issuer); with one issuer
+//           per tile the others keep the pipe fed;
 //   warps 2-5  epilogue: tcgen05.ld 32 columns at a time, masked running
 //           (max, argmax) per row -- a plain max when no tape is wanted -- then
 //           Sigma_t per query in t order, the normalisation and the `neg` fill;
@@ -56,12 +61,10 @@ namespace tc {
 
 constexpr int KBLK = 64;    // K elements per block: one 128-byte swizzled row
 constexpr int ROWB = 128;   // bytes per tile row
-constexpr int NWARPS = 7;
-constexpr int NTHREADS = NWARPS * 32;
 constexpr int SCHED_WARP = 6;
 constexpr int UQ = 16;      // metadata ring depth (units)
 constexpr int MW_MAX = 16;  // document-mask words carried per unit (Td <= 512)
-constexpr int QW_MAX = 8;   // query-row valid words (rows <= 256)
+constexpr int QW_MAX = 12;  // query-row valid words (rows <= 384)
 
 struct TcParams {
   ScanParams p;
@@ -199,8 +202,17 @@ __device__ __forceinline__ void mask_bits(const uint8_t* m, int n, uint32_t (&w)
 //         K blocks (one barrier round trip per chunk).  Without ARES (large dim)
 //         a stage carries one K block of both operands.
 //  SMAX   ring stages available (the launch uses as many as fit its budget).
+//  MAXMT = 3 (384 query rows, resident, one CTA per SM): the single
+//         accumulator is handed over tile by tile -- the MMA issuer fills tile m
+//         of the next chunk as soon as the epilogue has read tile m of this one,
+//         so the MMAs of one tile overlap the epilogue of the previous tile.
 template <int M, int NT, int MAXMT, int R, int NACC, int SMAX, int ARES>
 struct Cfg {
+  static constexpr bool TP = MAXMT == 3;            // tile-by-tile accumulator hand-off
+  static constexpr int NISS = MAXMT;                // MMA issuer warps: 1, then 7, 8
+  static constexpr int NTHR = (6 + NISS) * 32;      // producer, issuers, 4 epilogue, scheduler
+  static constexpr int MINB = TP ? 1 : 2;           // CTAs per SM
+  static constexpr int NBAR = TP ? MAXMT : NACC;    // accumulator barrier pairs
   static constexpr int A_BYTES = MAXMT * M * ROWB;  // one K block of all M tiles
   static constexpr int B_BYTES = NT * ROWB;         // one K block of a chunk
   static constexpr int ACC_COLS = MAXMT * NT;       // TMEM columns per accumulator buffer
@@ -214,6 +226,8 @@ struct Cfg {
                 "replication: 2 copies of 32 rows in a 64-row tile, or 4 in a 128-row tile");
   static_assert(TMEM_COLS % 128 == 0 && TMEM_COLS <= 512, "TMEM columns");
   static_assert(HALF % 32 == 0, "epilogue reads 32-column groups");
+  static_assert(!TP || (NACC == 1 && ARES == 1 && R == 1 && M == 128),
+                "tile hand-off: one accumulator, resident query, 128-row tiles");
 };
 
 struct BMaps {
@@ -231,10 +245,11 @@ __device__ __forceinline__ void load_doc_rows(unsigned char* sB, const BMaps& bm
   if (nr - r >= 16) { ptx::tma_load_2d(sB + r * ROWB, &bm.b16, x, (int)(row + r), bar); r += 16; }
 }
 
-// Every configuration runs two CTAs per SM (launch_cfg), so registers are
-// capped for two co-resident 224-thread CTAs.
+// Registers are capped for two co-resident CTAs, except for the three-tile
+// configuration (one CTA per SM).
 template <int M, int NT, int MAXMT, int R, int NACC, int SMAX, int ARES, bool ARGS>
-__global__ void __launch_bounds__(NTHREADS, 2)
+__global__ void __launch_bounds__(Cfg<M, NT, MAXMT, R, NACC, SMAX, ARES>::NTHR,
+                                  Cfg<M, NT, MAXMT, R, NACC, SMAX, ARES>::MINB)
 tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ BMaps bm, TcParams P,
                int S) {
   using L = Cfg<M, NT, MAXMT, R, NACC, SMAX, ARES>;
@@ -243,8 +258,8 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   __shared__ __align__(8) uint64_t empty_bar[SMAX];
   __shared__ __align__(8) uint64_t afull_bar[2];
   __shared__ __align__(8) uint64_t aempty_bar[2];
-  __shared__ __align__(8) uint64_t accf_bar[NACC];
-  __shared__ __align__(8) uint64_t acce_bar[NACC];
+  __shared__ __align__(8) uint64_t accf_bar[L::NBAR];
+  __shared__ __align__(8) uint64_t acce_bar[L::NBAR];
   __shared__ __align__(8) uint64_t metaf_bar[UQ];
   __shared__ __align__(8) uint64_t metae_bar[UQ];
   __shared__ __align__(8) uint64_t epi_bar;  // epilogue-wide barrier (bounded, unlike bar.sync);
@@ -270,21 +285,23 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   const ScanParams& p = P.p;
 
   if (threadIdx.x == 0) {
+    // every issuer commits to each ring slot, query slot and (without the tile
+    // hand-off) accumulator it uses
     for (int i = 0; i < SMAX; ++i) {
       ptx::mbar_init(&full_bar[i], 1);
-      ptx::mbar_init(&empty_bar[i], 1);
+      ptx::mbar_init(&empty_bar[i], L::NISS);
     }
     for (int i = 0; i < 2; ++i) {
       ptx::mbar_init(&afull_bar[i], 1);
-      ptx::mbar_init(&aempty_bar[i], 1);
+      ptx::mbar_init(&aempty_bar[i], L::NISS);
     }
-    for (int i = 0; i < NACC; ++i) {
-      ptx::mbar_init(&accf_bar[i], 1);
+    for (int i = 0; i < L::NBAR; ++i) {
+      ptx::mbar_init(&accf_bar[i], L::TP ? 1 : L::NISS);
       ptx::mbar_init(&acce_bar[i], 4);  // one arrival per epilogue warp
     }
     for (int i = 0; i < UQ; ++i) {
       ptx::mbar_init(&metaf_bar[i], 1);
-      ptx::mbar_init(&metae_bar[i], 6);  // producer + MMA + 4 epilogue warps
+      ptx::mbar_init(&metae_bar[i], 5 + L::NISS);  // producer + issuers + 4 epilogue warps
     }
     ptx::mbar_init(&epi_bar, 4);
     abort_s = 0;
@@ -473,8 +490,9 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         }
       }
     }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
+  } else if (warp == 1 || warp > SCHED_WARP) {
+    // ------------------------------------------------------------ MMA issuers
+    const int mo = warp == 1 ? 0 : warp - SCHED_WARP;  // this issuer's query tile
     int stage = 0;
     uint32_t phase = 0;
     int as = 0;
@@ -482,6 +500,7 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     int aslot = ARES - 1;
     uint32_t aslot_phase = 1;
     bool holding = false;    // ARES: an A slot is in use (released on the next switch)
+    uint32_t tph = 0;        // TP: phase of this tile's accumulator barriers
     for (int64_t i = 0;; ++i) {  // queued units, up to the end marker
       const int slot = (int)(i % UQ);
       if (!ptx::warp_wait(&metaf_bar[slot], (uint32_t)((i / UQ) & 1), &abort_s)) goto done;
@@ -501,38 +520,50 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         ptx::tc_fence_after();
         holding = true;
       }
+      const bool mine = mo < nmt;  // this unit has a tile for this issuer
       for (int c = 0; c < nch; ++c) {
         const int n = min(NT, leff - c * NT);
         const int nr = (n + 15) & ~15;
         const uint32_t idesc = ptx::idesc_f16(P.fmt, M, nr);
-        if (!ptx::warp_wait(&acce_bar[as], aphase ^ 1, &abort_s)) goto done;
-        ptx::tc_fence_after();
+        if (!L::TP) {
+          if (!ptx::warp_wait(&acce_bar[as], aphase ^ 1, &abort_s)) goto done;
+          ptx::tc_fence_after();
+        }
         for (int ks = 0; ks < spc; ++ks) {
           if (!ptx::warp_wait(&full_bar[stage], phase, &abort_s)) goto done;
           ptx::tc_fence_after();
+          if (L::TP && mine) {
+            // tile hand-off: the epilogue has released this tile's columns
+            if (!ptx::warp_wait(&acce_bar[mo], tph ^ 1u, &abort_s)) goto done;
+            ptx::tc_fence_after();
+          }
           if (lane == 0) {
-            const uint32_t st = ptx::smem_u32(ring + stage * sbytes);
-            for (int kk = 0; kk < kbs; ++kk) {
-              const int kb = ARES ? kk : ks;
-              const uint32_t sA = ARES ? ptx::smem_u32(aslots + aslot * abytes + kb * L::A_BYTES) : st;
-              const uint32_t sB = ARES ? st + kk * L::B_BYTES : st + L::A_BYTES;
-              const uint64_t bdesc = ptx::sw128_desc(sB);
-              for (int mt = 0; mt < nmt; ++mt) {
-                const uint64_t adesc = ptx::sw128_desc(sA + mt * M * ROWB);
-                const uint32_t d = tmem_base + (uint32_t)(as * L::ACC_COLS + mt * NT);
+            if (mine) {
+              const uint32_t st = ptx::smem_u32(ring + stage * sbytes);
+              const uint32_t d = tmem_base + (uint32_t)(as * L::ACC_COLS + mo * NT);
+              for (int kk = 0; kk < kbs; ++kk) {
+                const int kb = ARES ? kk : ks;
+                const uint32_t sA = ARES ? ptx::smem_u32(aslots + aslot * abytes + kb * L::A_BYTES) : st;
+                const uint32_t sB = ARES ? st + kk * L::B_BYTES : st + L::A_BYTES;
+                const uint64_t adesc = ptx::sw128_desc(sA + mo * M * ROWB);
+                const uint64_t bdesc = ptx::sw128_desc(sB);
 #pragma unroll
                 for (int k = 0; k < KBLK / 16; ++k)
                   ptx::mma_f16(d, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0);
               }
+              if (L::TP) ptx::mma_commit(&accf_bar[mo]);
             }
             ptx::mma_commit(&empty_bar[stage]);
           }
           __syncwarp();
+          if (L::TP && mine) tph ^= 1u;
           if (++stage == S) { stage = 0; phase ^= 1; }
         }
-        if (lane == 0) ptx::mma_commit(&accf_bar[as]);
-        __syncwarp();
-        if (++as == NACC) { as = 0; aphase ^= 1; }
+        if (!L::TP) {
+          if (lane == 0) ptx::mma_commit(&accf_bar[as]);
+          __syncwarp();
+          if (++as == NACC) { as = 0; aphase ^= 1; }
+        }
       }
     }
   } else {
@@ -549,6 +580,7 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     int as = 0;
     uint32_t aphase = 0;
     uint32_t ephase = 0;
+    uint32_t tph = 0;  // TP: bit mt = phase of tile mt's accumulator barriers
     float* scores = static_cast<float*>(p.scores);
     for (int64_t i = 0;; ++i) {  // queued units, up to the end marker
       const int slot = (int)(i % UQ);
@@ -591,54 +623,111 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           const int lim = n - col0;
           mw[g] = lim >= 32 ? w : (lim > 0 ? w & ((1u << lim) - 1u) : 0u);
         }
-        if (!ptx::warp_wait(&accf_bar[as], aphase, &abort_s)) goto done;
-        ptx::tc_fence_after();
+        if (!L::TP) {
+          if (!ptx::warp_wait(&accf_bar[as], aphase, &abort_s)) goto done;
+          ptx::tc_fence_after();
+        }
         const uint32_t tb = tmem_base + ((uint32_t)(sp * 32) << 16) + (uint32_t)(as * L::ACC_COLS);
         const int fc = first - u0 - h * L::HALF;  // first valid column, in my half?
         const bool s0_here = fc >= 0 && fc < L::HALF && first - u0 < n;
+        bool chunk_full = true;  // every column of the chunk valid (warp-uniform)
 #pragma unroll
-        for (int mt = 0; mt < MAXMT; ++mt) {
-          if (mt < nmt) {
+        for (int g = 0; g < L::HALF / 32; ++g) chunk_full = chunk_full && mw[g] == 0xffffffffu;
+        // one copy of the tile body (the running states of the tiles are
+        // selected in and out of registers): unrolling it per tile multiplies
+        // the epilogue's code, and instruction fetch then stalls it
+#pragma unroll 1
+        for (int mt = 0; mt < nmt; ++mt) {
+          float cmx = mx[0];
+          int cag = ag[0];
 #pragma unroll
-            for (int g = 0; g < L::HALF / 32; ++g) {
-              const int col0 = h * L::HALF + 32 * g;
-              if (col0 < n) {
-                uint32_t r[32];
-                ptx::tmem_ld32(tb + mt * NT + col0, r);
-                ptx::tmem_wait_ld();
-                const uint32_t mm = mw[g];
-                if (ARGS) {
+          for (int q = 1; q < MAXMT; ++q)
+            if (mt == q) { cmx = mx[q]; cag = ag[q]; }
+          if (L::TP) {
+            if (!ptx::warp_wait(&accf_bar[mt], (tph >> mt) & 1u, &abort_s)) goto done;
+            ptx::tc_fence_after();
+          }
+          // GB 32-column groups are loaded before one wait (all of a tile's
+          // groups with one CTA per SM; two when registers are shared).  The
+          // group code is branch-free apart from one warp-uniform test per tile
+          // (are all the chunk's columns valid?) and, with the tape, one vote
+          // per group: on this part a branch costs more than the dozens of
+          // selects it would skip.
+          constexpr int NG = L::HALF / 32;
+          constexpr int GB = L::TP ? NG : (NG < 2 ? NG : 2);
 #pragma unroll
-                  for (int cc = 0; cc < 32; ++cc) {
-                    const float s = __uint_as_float(r[cc]);
-                    if (((mm >> cc) & 1u) && s > mx[mt]) {
-                      mx[mt] = s;
-                      ag[mt] = u0 + col0 + cc + 1;
-                    }
-                  }
-                } else if (mm == 0xffffffffu) {
-                  // values only: max of the non-NaN entries (what strict `>` from
-                  // -inf keeps); the first-valid rule is applied at the end
+          for (int g0 = 0; g0 < NG; g0 += GB) {
+            uint32_t r[GB][32];
+            // columns past the chunk's end are read too (they lie inside this
+            // tile's accumulator) and masked out below
 #pragma unroll
-                  for (int cc = 0; cc < 32; ++cc) mx[mt] = fmaxf(mx[mt], __uint_as_float(r[cc]));
-                } else {
+            for (int gg = 0; gg < GB; ++gg) ptx::tmem_ld32(tb + mt * NT + h * L::HALF + 32 * (g0 + gg), r[gg]);
+            ptx::tmem_wait_ld();
+            if (!chunk_full) {
 #pragma unroll
-                  for (int cc = 0; cc < 32; ++cc)
-                    mx[mt] = fmaxf(mx[mt], ((mm >> cc) & 1u) ? __uint_as_float(r[cc]) : -INFINITY);
-                }
+              for (int gg = 0; gg < GB; ++gg) {
+                const uint32_t mm = mw[g0 + gg];
+#pragma unroll
+                for (int cc = 0; cc < 32; ++cc)
+                  r[gg][cc] = ((mm >> cc) & 1u) ? r[gg][cc] : __float_as_uint(-INFINITY);
               }
             }
-            if (s0_here) {
-              s0[mt] = __uint_as_float(ptx::tmem_ld1(tb + mt * NT + (first - u0)));
-              ptx::tmem_wait_ld();
-              has_s0 = true;
+#pragma unroll
+            for (int gg = 0; gg < GB; ++gg) {
+              // max of the group's valid non-NaN entries: four interleaved
+              // chains of three-input maxima (NaN inputs are dropped, so the
+              // order does not matter); masked columns hold -inf
+              float t4[4] = {ARGS ? -INFINITY : cmx, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+              for (int cc = 0; cc < 32; cc += 2)
+                t4[(cc >> 1) & 3] = ptx::fmax3(t4[(cc >> 1) & 3], __uint_as_float(r[gg][cc]),
+                                               __uint_as_float(r[gg][cc + 1]));
+              const float gmax = fmaxf(fmaxf(t4[0], t4[1]), fmaxf(t4[2], t4[3]));
+              if (ARGS) {
+                // the running (max, argmax) of a strict `>` scan in column
+                // order: the group wins only with a strictly larger value, and
+                // its argmax is the first column holding that value (a masked
+                // column holds -inf, which never wins)
+                if (__any_sync(0xffffffffu, gmax > cmx)) {
+                  int idx = 31;
+#pragma unroll
+                  for (int cc = 30; cc >= 0; --cc) idx = (__uint_as_float(r[gg][cc]) == gmax) ? cc : idx;
+                  const bool take = gmax > cmx;
+                  cag = take ? u0 + h * L::HALF + 32 * (g0 + gg) + idx + 1 : cag;
+                  cmx = take ? gmax : cmx;
+                }
+              } else {
+                // values only; the first-valid rule is applied at the end
+                cmx = gmax;
+              }
             }
           }
+          float cs0 = 0.f;
+          if (s0_here) {
+            cs0 = __uint_as_float(ptx::tmem_ld1(tb + mt * NT + (first - u0)));
+            ptx::tmem_wait_ld();
+            has_s0 = true;
+          }
+#pragma unroll
+          for (int q = 0; q < MAXMT; ++q)
+            if (mt == q) {
+              mx[q] = cmx;
+              ag[q] = cag;
+              if (s0_here) s0[q] = cs0;
+            }
+          if (L::TP) {
+            ptx::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive(&acce_bar[mt]);
+            tph ^= 1u << mt;
+          }
         }
-        ptx::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(&acce_bar[as]);
-        if (++as == NACC) { as = 0; aphase ^= 1; }
+        if (!L::TP) {
+          ptx::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) ptx::mbar_arrive(&acce_bar[as]);
+          if (++as == NACC) { as = 0; aphase ^= 1; }
+        }
       }
       if (R > 1) {
         // copies 1..R-1 of rows 0-31 (the other column slices) hand their states over
@@ -801,14 +890,18 @@ static int queries_total(const ScanParams& p) {
   return p.layout == L_INBATCH ? p.Bq : (p.layout == L_PACKED ? p.nq : 1);
 }
 
-// Queries stacked per unit and the resulting row count (up to 256 rows in two
-// 128-row tiles; at most 128 queries, one epilogue thread sums each).
+// Largest stacked row count: three resident 128-row tiles when the query's K
+// blocks fit (dim <= 128: 96 KB of query tile), else two tiles carried per stage.
+static int max_rows(const ScanParams& p) { return p.dim <= 2 * KBLK ? 384 : 256; }
+
+// Queries stacked per unit and the resulting row count (up to max_rows(); at
+// most 128 queries, one epilogue thread sums each).
 static void plan(const ScanParams& p, int& G, int& rows) {
   const int Tq = p.Tq;
   G = 1;
   if ((p.layout == L_INBATCH || p.layout == L_PACKED) && Tq > 0) {
     const int nq = queries_total(p);
-    G = 256 / Tq;
+    G = max_rows(p) / Tq;
     if (G < 1) G = 1;
     if (G > 128) G = 128;
     if (G > nq) G = nq > 0 ? nq : 1;
@@ -837,7 +930,7 @@ static cudaError_t launch_cfg(const TcParams& P, const CUtensorMap& a, const BMa
   int64_t grid = (int64_t)device_sm_count() * ctas_per_sm;
   if (grid > P.nunits) grid = P.nunits;
   if (grid < 1) grid = 1;
-  k<<<(unsigned)grid, NTHREADS, dyn, s>>>(a, bm, P, S);
+  k<<<(unsigned)grid, L::NTHR, dyn, s>>>(a, bm, P, S);
   return cudaGetLastError();
 }
 
@@ -894,7 +987,7 @@ bool scan_tc_supported(int dtype, const ScanParams& p) {
   if (p.Tq <= 0) return false;
   int G, rows;
   tc::plan(p, G, rows);
-  return rows <= 256;
+  return rows <= tc::max_rows(p);
 }
 
 cudaError_t launch_scan_tc(int dtype, const ScanParams& p, cudaStream_t s) {
@@ -931,6 +1024,8 @@ cudaError_t launch_scan_tc(int dtype, const ScanParams& p, cudaStream_t s) {
     return tc::launch_cfg<128, 256, 1, 4, 1, 2, 0>(P, a, bm, s, 2, B2);
   if (rows <= 64) return tc::launch_auto<64, 64, 1, 1, 4, 8>(P, a, bm, s, 2, B2);
   if (rows <= 128) return tc::launch_auto<128, 64, 1, 1, 4, 8>(P, a, bm, s, 2, B2);
+  if (rows > 256)  // three resident tiles, one CTA per SM, tile-by-tile accumulator hand-off
+    return tc::launch_cfg<128, 128, 3, 1, 1, 4, 1>(P, a, bm, s, 1, 200 * 1024);
   // two 128-row tiles: two CTAs per SM, one 256-column accumulator each (two
   // MMA issuers and epilogues per SM beat one CTA with two accumulators)
   return tc::launch_auto<128, 128, 2, 1, 1, 12>(P, a, bm, s, 2, B2);

@@ -163,6 +163,15 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
                : "memory");
 }
 
+// Three-input maximum (sm_100 max.f32 with three sources): the largest
+// non-NaN input, NaN only when all three are NaN -- two-input fmaxf applied
+// twice, in one instruction.
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // 32 consecutive columns of this warp's 32 TMEM lanes -> 32 registers per thread.

@@ -41,9 +41,12 @@ def test_candidates_c2_like(fms, oracle, dtype, args_on):
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-def test_inbatch_c3_like(fms, oracle, dtype):
+@pytest.mark.parametrize("Bq,dim", [(12, 768), (20, 128), (13, 64)])
+def test_inbatch_c3_like(fms, oracle, dtype, Bq, dim):
+    """dim 768: two 128-row query tiles carried per K block; dim <= 128: up to
+    twelve 32-token queries (three resident tiles) per unit, in two groups."""
     g = torch.Generator().manual_seed(3)
-    Bq, Bd, Tq, Td, dim = 12, 10, 32, 180, 768
+    Bd, Tq, Td = 10, 32, 180
     Q = l2t(torch.randn(Bq, Tq, dim, generator=g)).to(dtype).cuda()
     D = l2t(torch.randn(Bd, Td, dim, generator=g)).to(dtype).cuda()
     lens = torch.randint(32, Td + 1, (Bd,), generator=g)
@@ -91,11 +94,13 @@ def test_paired_row_configs(fms, oracle, Tq, Td):
     assert_args(a.cpu(), ao, lambda i, u: sims(Qc[i[0]], Dc[i[0]])[i[1], u - 1], 1e-3)
 
 
-@pytest.mark.parametrize("nq,Tq", [(16, 24), (40, 24), (13, 30)])
+@pytest.mark.parametrize("nq,Tq", [(16, 24), (40, 24), (13, 30), (11, 24)])
 def test_packed_query_groups(fms, oracle, nq, Tq):
-    """Packed scans whose stacked queries exceed one unit's 256 rows run in
-    several query groups (the last one partial); query masks, a fully masked
-    query and normalisation included."""
+    """Stacked queries up to 384 rows per unit at dim 128 (three resident
+    128-row tiles, the accumulator handed over tile by tile); more queries run
+    in several groups, the last one partial (fewer tiles than the first);
+    query masks, a fully masked query, normalisation, and the values-only scan
+    (no tape) included."""
     g = torch.Generator().manual_seed(nq * Tq)
     dim = 128
     lens = torch.randint(1, 400, (23,), generator=g).tolist()
@@ -112,6 +117,8 @@ def test_packed_query_groups(fms, oracle, nq, Tq):
         Qc, tok, cu = Qs.cpu(), P.tokens.cpu(), P.cu.cpu().numpy()
         assert_args(A.cpu(), Ao,
                     lambda i, u: sims(Qc[i[0]], tok[cu[i[1]] - 1:cu[i[1] + 1] - 1])[i[2], u - 1], 1e-3)
+        S2, _ = fms.packed_forward(Qs, P, qm.cuda(), normalize=normalize, want_args=False)
+        assert torch.equal(S2, S)
 
 
 def test_stacked_single_token_queries(fms, oracle):
@@ -128,3 +135,30 @@ def test_stacked_single_token_queries(fms, oracle):
     P = fms.pack_docs(docs)
     S2, _ = fms.packed_forward(Q, P)
     assert_scores(S2.cpu(), So, 1e-3)
+
+
+@pytest.mark.parametrize("nq,Tq,dim", [(16, 24, 128), (8, 32, 768)])
+@pytest.mark.parametrize("want", [True, False])
+def test_packed_nan_first_column_sticks(fms, oracle, nq, Tq, dim, want):
+    """forward_pair.jl:83 (`arg == 0 || s > mx`) on the stacked-query engine
+    (three resident tiles at dim 128, two carried tiles at dim 768): a NaN
+    similarity at a document's first token is the result for every query row;
+    a NaN at a later token (in a later 128-token chunk) never wins."""
+    g = torch.Generator().manual_seed(nq + dim)
+    lens = [300, 260, 140, 90]
+    docs = [l2t(torch.randn(n, dim, generator=g)).half() for n in lens]
+    docs[1][0, 0] = float("nan")      # first token of document 2
+    docs[2][130, 3] = float("nan")    # a later token of document 3 (second chunk)
+    P = fms.pack_docs([d.cuda() for d in docs])
+    Qs = l2t(torch.randn(nq, Tq, dim, generator=g)).half().cuda()
+    S, A = fms.packed_forward(Qs, P, want_args=want)
+    So, Ao = oracle.packed(Qs, P.tokens, P.cu.cpu())
+    S = S.cpu()
+    assert torch.isnan(S[:, 1]).all() and torch.isfinite(S[:, [0, 2, 3]]).all()
+    assert_scores(S, So, 1e-3)
+    if want:
+        A = A.cpu()
+        assert (A[:, 1] == 1).all() and (A[:, 2] != 131).all()
+        Qc, tok, cu = Qs.cpu(), P.tokens.cpu(), P.cu.cpu().numpy()
+        assert_args(A, Ao, lambda i, u: sims(Qc[i[0]], tok[cu[i[1]] - 1:cu[i[1] + 1] - 1])[i[2], u - 1],
+                    1e-3)
