@@ -132,31 +132,26 @@ __device__ __forceinline__ uint32_t tmem_ld1_sync(uint32_t taddr) {
   return r;
 }
 
-// Masked max of the dequantised scores of 32 columns (one thread = one query
-// token): s = (qs * ds_u) * float(acc_u), float(acc) = bits - 12582912 exactly.
+// Max of the dequantised scores of 32 columns (one thread = one query token):
+// s = (qs * ds_u) * (acc_bits - 12582912), paired f32x2, three-input maxima.
+// FULL: every column valid; otherwise the mask word selects (-inf elsewhere).
+// Branch-free: on this part a branch costs more than the selects it skips.
+template <bool FULL>
 __device__ __forceinline__ void reduce32(const uint32_t (&r)[32], uint32_t mm, const float* ds, float2 qs2,
                                          float& mx0, float& mx1) {
   const float2 negm = make_float2(-MAGIC_F, -MAGIC_F);
   const float4* dsp = reinterpret_cast<const float4*>(ds);
-  if (mm == 0xffffffffu) {
 #pragma unroll
-    for (int q4 = 0; q4 < 8; ++q4) {
-      const float4 dv = dsp[q4];
-      const float2 a0 = __fadd2_rn(make_float2(__uint_as_float(r[4 * q4]), __uint_as_float(r[4 * q4 + 1])), negm);
-      const float2 a1 = __fadd2_rn(make_float2(__uint_as_float(r[4 * q4 + 2]), __uint_as_float(r[4 * q4 + 3])), negm);
-      const float2 s0 = __fmul2_rn(__fmul2_rn(qs2, make_float2(dv.x, dv.y)), a0);
-      const float2 s1 = __fmul2_rn(__fmul2_rn(qs2, make_float2(dv.z, dv.w)), a1);
+  for (int q4 = 0; q4 < 8; ++q4) {
+    const float4 dv = dsp[q4];
+    const float2 a0 = __fadd2_rn(make_float2(__uint_as_float(r[4 * q4]), __uint_as_float(r[4 * q4 + 1])), negm);
+    const float2 a1 = __fadd2_rn(make_float2(__uint_as_float(r[4 * q4 + 2]), __uint_as_float(r[4 * q4 + 3])), negm);
+    const float2 s0 = __fmul2_rn(__fmul2_rn(qs2, make_float2(dv.x, dv.y)), a0);
+    const float2 s1 = __fmul2_rn(__fmul2_rn(qs2, make_float2(dv.z, dv.w)), a1);
+    if (FULL) {
       mx0 = max3(mx0, s0.x, s0.y);
       mx1 = max3(mx1, s1.x, s1.y);
-    }
-  } else if (mm != 0u) {
-#pragma unroll
-    for (int q4 = 0; q4 < 8; ++q4) {
-      const float4 dv = dsp[q4];
-      const float2 a0 = __fadd2_rn(make_float2(__uint_as_float(r[4 * q4]), __uint_as_float(r[4 * q4 + 1])), negm);
-      const float2 a1 = __fadd2_rn(make_float2(__uint_as_float(r[4 * q4 + 2]), __uint_as_float(r[4 * q4 + 3])), negm);
-      const float2 s0 = __fmul2_rn(__fmul2_rn(qs2, make_float2(dv.x, dv.y)), a0);
-      const float2 s1 = __fmul2_rn(__fmul2_rn(qs2, make_float2(dv.z, dv.w)), a1);
+    } else {
       const uint32_t b4 = mm >> (4 * q4);
       mx0 = max3(mx0, (b4 & 1u) ? s0.x : -INFINITY, (b4 & 2u) ? s0.y : -INFINITY);
       mx1 = max3(mx1, (b4 & 4u) ? s1.x : -INFINITY, (b4 & 8u) ? s1.y : -INFINITY);
@@ -164,6 +159,25 @@ __device__ __forceinline__ void reduce32(const uint32_t (&r)[32], uint32_t mm, c
   }
 }
 
+// Masked max over one document slot of W 32-column groups (W compile-time, so
+// the loop has no runtime bounds).  One 32-register buffer: a TMEM load
+// completes in a few dozen cycles, and a second buffer would not fit the 96
+// registers that 18 warps per SM leave each thread.
+template <int W, bool FULL>
+__device__ __forceinline__ void reduce_doc(uint32_t tcol, const uint32_t* mw, const float* ds, float2 qs2,
+                                           float& mx0, float& mx1) {
+#pragma unroll 1
+  for (int w = 0; w < W; ++w) {
+    uint32_t r[32];
+    ptx::tmem_ld32(tcol + 32 * w, r);
+    tmem_wait_ld_regs(r);
+    reduce32<FULL>(r, FULL ? 0u : mw[w], ds + 32 * w, qs2, mx0, mx1);
+  }
+}
+
+// W: 32-column groups per document slot (Td rounded up to 32, / 32), a
+// template parameter so that the epilogue's per-document loop is unrolled.
+template <int W>
 __global__ void __launch_bounds__(NTHREADS, 1)
 i8_exhaustive_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmG,
                      Params P) {
@@ -309,11 +323,12 @@ i8_exhaustive_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
           for (int c = lane; c < P.Tdp; c += 32)
             ds_s[s][d * P.Tdp + c] = c < P.Td ? ld_scale(P.Gs, P.ds_f16, j * P.Td + c) : 0.f;
           first = -1;
-          for (int w = 0; w < P.W; ++w) {
+#pragma unroll 1
+          for (int w = 0; w < W; ++w) {
             const int c = 32 * w + lane;
             const bool ok = c < P.Td && (P.dmask == nullptr || P.dmask[j * P.Td + c] != 0);
             const uint32_t word = __ballot_sync(0xffffffffu, ok);
-            if (lane == 0) mw_s[s][d * P.W + w] = word;
+            if (lane == 0) mw_s[s][d * W + w] = word;
             if (first < 0 && word != 0u) first = 32 * w + __ffs(word) - 1;
           }
         }
@@ -405,21 +420,13 @@ i8_exhaustive_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
             const int cbase = (d - u * P.dpu) * P.Tdp;  // column within the accumulator
             const int sbase = d * P.Tdp;                // column within the stage
             float mx0 = -INFINITY, mx1 = -INFINITY;
-            // 32-column groups, the next group's TMEM load in flight while the
-            // current one is reduced
-            uint32_t ra[32], rb[32];
-            ptx::tmem_ld32(tacc + cbase, ra);
-            tmem_wait_ld_regs(ra);
-            for (int w = 0; w < P.W; w += 2) {
-              if (w + 1 < P.W) ptx::tmem_ld32(tacc + cbase + 32 * (w + 1), rb);
-              reduce32(ra, mw_s[s][d * P.W + w], &ds_s[s][sbase + 32 * w], qs2, mx0, mx1);
-              if (w + 1 < P.W) {
-                tmem_wait_ld_regs(rb);
-                if (w + 2 < P.W) ptx::tmem_ld32(tacc + cbase + 32 * (w + 2), ra);
-                reduce32(rb, mw_s[s][d * P.W + w + 1], &ds_s[s][sbase + 32 * (w + 1)], qs2, mx0, mx1);
-                if (w + 2 < P.W) tmem_wait_ld_regs(ra);
-              }
-            }
+            // one warp-uniform test per document: all its columns valid?
+            const uint32_t* mwd = &mw_s[s][d * W];
+            bool full = true;
+#pragma unroll
+            for (int w = 0; w < W; ++w) full = full && mwd[w] == 0xffffffffu;
+            if (full) reduce_doc<W, true>(tacc + cbase, mwd, &ds_s[s][sbase], qs2, mx0, mx1);
+            else reduce_doc<W, false>(tacc + cbase, mwd, &ds_s[s][sbase], qs2, mx0, mx1);
             const float mx = fmaxf(mx0, mx1);
             float v = 0.f;
             if (first >= 0) {
@@ -558,9 +565,21 @@ cudaError_t launch_int8_exhaustive_tc(const Int8ScanParams& p, cudaStream_t s) {
     // the whole budget, whatever this pass needs: one CTA per SM, so that the
     // 512-column TMEM allocation never waits for a co-resident CTA
     const int dyn = SMEM_BUDGET;
-    cudaError_t e = cudaFuncSetAttribute(i8_exhaustive_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn);
+    void (*k)(const CUtensorMap, const CUtensorMap, Params) = nullptr;
+    switch (P.W) {
+      case 1: k = i8_exhaustive_kernel<1>; break;
+      case 2: k = i8_exhaustive_kernel<2>; break;
+      case 3: k = i8_exhaustive_kernel<3>; break;
+      case 4: k = i8_exhaustive_kernel<4>; break;
+      case 5: k = i8_exhaustive_kernel<5>; break;
+      case 6: k = i8_exhaustive_kernel<6>; break;
+      case 7: k = i8_exhaustive_kernel<7>; break;
+      case 8: k = i8_exhaustive_kernel<8>; break;
+      default: return cudaErrorNotSupported;
+    }
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn);
     if (e != cudaSuccess) return e;
-    i8_exhaustive_kernel<<<(unsigned)grid, NTHREADS, dyn, s>>>(tq, tg, P);
+    k<<<(unsigned)grid, NTHREADS, dyn, s>>>(tq, tg, P);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   return cudaSuccess;

@@ -509,9 +509,9 @@ gallery_kernel(const __grid_constant__ Maps maps, Params P) {
             if (m.mw_ok || u < 32 * MW_MAX) ok = (m.mw[u >> 5] >> (u & 31)) & 1u;
             else ok = m.dmask == nullptr || m.dmask[u] != 0;
           }
-          const bool any = __any_sync(0xffffffffu, ok);
+          // no early exit for 32 rows without a valid token: they are rare, and
+          // on this part a branch costs about as much as the selects below
           const bool has_first = __any_sync(0xffffffffu, u == first);
-          if (!any && !has_first) continue;  // warp-uniform: nothing valid in these 32 rows
           uint32_t r[32];
           ptx::tmem_ld32(tmem_base + ((uint32_t)(sp * 32) << 16) + a * (uint32_t)P.acc_cols +
                              (uint32_t)(t * NQ),
@@ -525,11 +525,10 @@ gallery_kernel(const __grid_constant__ Maps maps, Params P) {
             for (int j = 0; j < (I8 ? 32 : 1); ++j)
               r[j] = __float_as_uint((qsr[j] * dsu) * __int2float_rn((int)r[j]));
           }
-          if (u == first) {
+          if (has_first && u == first) {
 #pragma unroll
             for (int j = 0; j < 32; ++j) s0_s[g][par][j] = __uint_as_float(r[j]);
           }
-          if (!any) continue;
           float v[32];
           if (ARGS) {
             int ai[32];
