@@ -211,7 +211,7 @@ struct Cfg {
   static constexpr bool TP = MAXMT == 3;            // tile-by-tile accumulator hand-off
   static constexpr int NISS = MAXMT;                // MMA issuer warps: 1, then 7, 8
   static constexpr int NTHR = (6 + NISS) * 32;      // producer, issuers, 4 epilogue, scheduler
-  static constexpr int MINB = TP ? 1 : 2;           // CTAs per SM
+  static constexpr int MINB = NACC * MAXMT * NT > 256 ? 1 : 2;  // CTAs per SM (TMEM: 512 columns)
   static constexpr int NBAR = TP ? MAXMT : NACC;    // accumulator barrier pairs
   static constexpr int A_BYTES = MAXMT * M * ROWB;  // one K block of all M tiles
   static constexpr int B_BYTES = NT * ROWB;         // one K block of a chunk
@@ -647,14 +647,14 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             if (!ptx::warp_wait(&accf_bar[mt], (tph >> mt) & 1u, &abort_s)) goto done;
             ptx::tc_fence_after();
           }
-          // GB 32-column groups are loaded before one wait (all of a tile's
-          // groups with one CTA per SM; two when registers are shared).  The
+          // GB 32-column groups are loaded before one wait (three or four with
+          // one CTA per SM; two when registers are shared).  The
           // group code is branch-free apart from one warp-uniform test per tile
           // (are all the chunk's columns valid?) and, with the tape, one vote
           // per group: on this part a branch costs more than the dozens of
           // selects it would skip.
           constexpr int NG = L::HALF / 32;
-          constexpr int GB = L::TP ? NG : (NG < 2 ? NG : 2);
+          constexpr int GB = L::MINB == 1 ? (NG % 3 == 0 ? 3 : (NG < 4 ? NG : 4)) : (NG < 2 ? NG : 2);
 #pragma unroll
           for (int g0 = 0; g0 < NG; g0 += GB) {
             uint32_t r[GB][32];
@@ -1027,7 +1027,9 @@ cudaError_t launch_scan_tc(int dtype, const ScanParams& p, cudaStream_t s) {
   if (rows > 256)  // three resident tiles, one CTA per SM, tile-by-tile accumulator hand-off
     return tc::launch_cfg<128, 128, 3, 1, 1, 4, 1>(P, a, bm, s, 1, 200 * 1024);
   // two 128-row tiles: two CTAs per SM, one 256-column accumulator each (two
-  // MMA issuers and epilogues per SM beat one CTA with two accumulators)
+  // CTAs' issuers and epilogues per SM beat one CTA with wider 192-row chunks,
+  // which would bring the stacked query once per 192 document rows but leaves
+  // no accumulator for the MMAs to run ahead into)
   return tc::launch_auto<128, 128, 2, 1, 1, 12>(P, a, bm, s, 2, B2);
 }
 

@@ -249,3 +249,28 @@ def test_candidates_invgrid_million_destinations(fms, oracle):
     dQo, dGo = oracle.candidates_pullback(Delta.to(dtype), None, Q, G, idxs, None, args.cpu(), 1, 2)
     close(dQ, dQo, 1e-2, "dQ")
     close(dG, dGo, 1e-2, "dG")
+
+
+@pytest.mark.parametrize("dtype,dim", [(torch.bfloat16, 768), (torch.float16, 64), (torch.float32, 96)])
+def test_inbatch_invgrid_many_documents(fms, oracle, dtype, dim):
+    """InvGrid dQ of in-batch scans with more documents than one 16-document
+    batch of the bulk-copy row ring (40 documents: three batches, the last one
+    partial), masked query tokens (zero rows) and masked document tokens;
+    against the oracle pullback, and bit-identical on a second call."""
+    rng = seeded(61 + dim)
+    Bq, Bd, Tq, Td = 5, 40, 8, 30
+    Q, D = feats(rng, (Bq, Tq, dim), dtype), feats(rng, (Bd, Td, dim), dtype)
+    qm = torch.from_numpy(rng.random((Bq, Tq)) > 0.2).cuda()
+    lens = rng.integers(1, Td + 1, Bd)
+    dm = torch.from_numpy(np.arange(Td)[None, :] < lens[:, None]).cuda()
+    _, args = fms.inbatch_forward(Q, D, qm, dm)
+    Delta = torch.randn(Bq, Bd, device="cuda").to(dtype)
+    dQ, dD = fms.inbatch_pullback(Delta, Q, D, qm, args, None, fms.InvGrid())
+    dcode = {torch.bfloat16: 2, torch.float16: 1, torch.float32: 0}[dtype]
+    dQo, dDo = oracle.inbatch_pullback(Delta, None, Q, D, qm.cpu(), args.cpu(), 1, dcode)
+    tol = 1e-5 if dtype == torch.float32 else 1e-2
+    close(dQ, dQo, tol, "dQ")
+    close(dD, dDo, tol, "dD")
+    assert (dQ[~qm] == 0).all()
+    dQ2, dD2 = fms.inbatch_pullback(Delta, Q, D, qm, args, None, fms.InvGrid())
+    assert torch.equal(dQ, dQ2) and torch.equal(dD, dD2)
