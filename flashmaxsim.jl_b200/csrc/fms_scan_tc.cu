@@ -526,15 +526,15 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const int nr = (n + 15) & ~15;
         const uint32_t idesc = ptx::idesc_f16(P.fmt, M, nr);
         if (!L::TP) {
-          if (!ptx::warp_wait(&acce_bar[as], aphase ^ 1, &abort_s)) goto done;
+          if (!ptx::all_wait(&acce_bar[as], aphase ^ 1, &abort_s)) goto done;
           ptx::tc_fence_after();
         }
         for (int ks = 0; ks < spc; ++ks) {
-          if (!ptx::warp_wait(&full_bar[stage], phase, &abort_s)) goto done;
+          if (!ptx::all_wait(&full_bar[stage], phase, &abort_s)) goto done;
           ptx::tc_fence_after();
           if (L::TP && mine) {
             // tile hand-off: the epilogue has released this tile's columns
-            if (!ptx::warp_wait(&acce_bar[mo], tph ^ 1u, &abort_s)) goto done;
+            if (!ptx::all_wait(&acce_bar[mo], tph ^ 1u, &abort_s)) goto done;
             ptx::tc_fence_after();
           }
           if (lane == 0) {
@@ -624,7 +624,7 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           mw[g] = lim >= 32 ? w : (lim > 0 ? w & ((1u << lim) - 1u) : 0u);
         }
         if (!L::TP) {
-          if (!ptx::warp_wait(&accf_bar[as], aphase, &abort_s)) goto done;
+          if (!ptx::all_wait(&accf_bar[as], aphase, &abort_s)) goto done;
           ptx::tc_fence_after();
         }
         const uint32_t tb = tmem_base + ((uint32_t)(sp * 32) << 16) + (uint32_t)(as * L::ACC_COLS);
@@ -644,7 +644,7 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           for (int q = 1; q < MAXMT; ++q)
             if (mt == q) { cmx = mx[q]; cag = ag[q]; }
           if (L::TP) {
-            if (!ptx::warp_wait(&accf_bar[mt], (tph >> mt) & 1u, &abort_s)) goto done;
+            if (!ptx::all_wait(&accf_bar[mt], (tph >> mt) & 1u, &abort_s)) goto done;
             ptx::tc_fence_after();
           }
           // GB 32-column groups are loaded before one wait (three or four with

@@ -100,6 +100,14 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
   return ok != 0;
 }
 
+// Warp-wide bounded wait in which every lane polls the barrier itself: a phase
+// that has already completed costs one poll per lane, with no broadcast from a
+// single polling lane; the verdict is warp-uniform.
+__device__ __forceinline__ bool all_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  const bool ok = mbar_wait(bar, parity, abort);
+  return __all_sync(0xffffffffu, ok);
+}
+
 // 2-D TMA tile load (coordinates: x = innermost element, y = row).
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
                                             uint64_t* bar) {
