@@ -14,8 +14,8 @@
 // each stage up to 256 document rows (two 128-token documents).
 //
 // Warp roles (576 threads, one CTA per SM, persistent over a contiguous range
-// of stages; the producer and the MMA lane sleep in their waits, the epilogue
-// warps spin):
+// of stages; the producer sleeps in its waits, the MMA lane spins on the
+// accumulators (sleeps on the stages), every epilogue lane polls its barriers):
 //   warp 0  producer: TMA loads of the document rows, plus the stage's
 //           document scales and mask words written to shared memory by all 32
 //           lanes (every lane arrives on the stage barrier after its stores);
@@ -364,7 +364,7 @@ i8_exhaustive_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
             const int nd = min(P.dpu, ndoc - u * P.dpu);
             const int n = nd * P.Tdp;  // MMA N: a multiple of 32, at most UW
             // the first use of each buffer passes at once (parity of the phase before)
-            if (!ptx::mbar_wait<true>(&acce_bar[b], (use & 1u) ^ 1u, &abort_s)) goto mma_out;
+            if (!ptx::mbar_wait(&acce_bar[b], (use & 1u) ^ 1u, &abort_s)) goto mma_out;
             ptx::tc_fence_after();
             const uint32_t d = tmem_base + b * (uint32_t)P.UW;
             // every accumulator entry <- 12582912.0f (bits 0x4B400000), then the
@@ -398,7 +398,7 @@ i8_exhaustive_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
     for (int64_t i = 0; i < my_st; ++i) {
       const int s = (int)(i & (STAGES - 1));
       const uint32_t ph = (uint32_t)((i / STAGES) & 1);
-      if (!ptx::warp_wait(&full_bar[s], ph, &abort_s)) goto done;
+      if (!ptx::all_wait(&full_bar[s], ph, &abort_s)) goto done;
       const int64_t j0 = (st_begin + i) * P.dps;
       int ndoc = P.dps;
       if (j0 + ndoc > P.N) ndoc = (int)(P.N - j0);
@@ -408,7 +408,7 @@ i8_exhaustive_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
         for (int u = 0; u < nunit; ++u, ++c) {
           if ((int)(c & ((1u << nbl) - 1u)) != g) continue;
           const uint32_t use = c >> nbl;
-          if (!ptx::warp_wait(&accf_bar[g], use & 1u, &abort_s)) goto done;
+          if (!ptx::all_wait(&accf_bar[g], use & 1u, &abort_s)) goto done;
           ptx::tc_fence_after();
           const float qsv = qs_s[qi][lane];
           const uint32_t qv = qv_s[qi];
