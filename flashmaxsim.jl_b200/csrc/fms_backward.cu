@@ -493,34 +493,53 @@ __device__ __forceinline__ void inb_gather_row(const BwdParams& b, int64_t r, in
       else my_a = 0;
     }
     const int nd = (int)min((int64_t)32, p.Bd - j0);
-    for (int d0 = 0; d0 < nd; d0 += GB_ROWS) {
-      int a[GB_ROWS];
-      float dl[GB_ROWS];
-      uint4 dv[GB_ROWS][NV];
+    if (nd == 32 && __all_sync(0xffffffffu, my_a != 0)) {
+      // every document of the batch contributes: no per-row tests (a branch
+      // costs more here than the loads and FMAs it guards)
+#pragma unroll 1
+      for (int d0 = 0; d0 < 32; d0 += GB_ROWS) {
+        float dl[GB_ROWS];
+        uint4 dv[GB_ROWS][NV];
 #pragma unroll
-      for (int q = 0; q < GB_ROWS; ++q) {
-        a[q] = __shfl_sync(0xffffffffu, my_a, (d0 + q) & 31);
-        dl[q] = __shfl_sync(0xffffffffu, my_dl, (d0 + q) & 31);
-        if (d0 + q >= nd) a[q] = 0;
-        const int64_t drow = (j0 + d0 + q) * p.Td + a[q] - 1;
+        for (int q = 0; q < GB_ROWS; ++q) {
+          const int aq = __shfl_sync(0xffffffffu, my_a, d0 + q);
+          dl[q] = __shfl_sync(0xffffffffu, my_dl, d0 + q);
+          const int64_t drow = (j0 + d0 + q) * p.Td + aq - 1;
 #pragma unroll
-        for (int k = 0; k < NV; ++k) {
-          const int v = lane + 32 * k;
-          if (a[q] && v < nvec) dv[q][k] = D[drow * nvec + v];
-        }
-      }
-#pragma unroll
-      for (int q = 0; q < GB_ROWS; ++q) {
-        if (!a[q]) continue;
-#pragma unroll
-        for (int k = 0; k < NV; ++k) {
-          const int v = lane + 32 * k;
-          if (v < nvec) {
-            float x[E];
-            unpack(dv[q][k], x, (T*)nullptr);
-#pragma unroll
-            for (int e = 0; e < E; ++e) acc[k][e] += dl[q] * x[e];
+          for (int k = 0; k < NV; ++k) {
+            const int v = lane + 32 * k;
+            if (v < nvec) dv[q][k] = D[drow * nvec + v];
           }
+        }
+#pragma unroll
+        for (int q = 0; q < GB_ROWS; ++q)
+#pragma unroll
+          for (int k = 0; k < NV; ++k) {
+            const int v = lane + 32 * k;
+            if (v < nvec) {
+              float x[E];
+              unpack(dv[q][k], x, (T*)nullptr);
+#pragma unroll
+              for (int e = 0; e < E; ++e) acc[k][e] += dl[q] * x[e];
+            }
+          }
+      }
+      continue;
+    }
+    // a partial batch (the last one, or invalid tape entries): one row at a time
+    for (int d = 0; d < nd; ++d) {
+      const int ad = __shfl_sync(0xffffffffu, my_a, d);
+      const float dl = __shfl_sync(0xffffffffu, my_dl, d);
+      if (!ad) continue;
+      const int64_t drow = (j0 + d) * p.Td + ad - 1;
+#pragma unroll
+      for (int k = 0; k < NV; ++k) {
+        const int v = lane + 32 * k;
+        if (v < nvec) {
+          float x[E];
+          unpack(D[drow * nvec + v], x, (T*)nullptr);
+#pragma unroll
+          for (int e = 0; e < E; ++e) acc[k][e] += dl * x[e];
         }
       }
     }
@@ -664,24 +683,27 @@ csr_scatter_vec_kernel(BwdParams b, const int32_t* __restrict__ row_ptr, const i
         }
       }
       const int ns = min(32, n - i0);
+      // SC_ROWS rows in flight; rows past the batch end read row 0 and are
+      // discarded by a select (a per-row branch costs more than the selects)
+#pragma unroll 1
       for (int c0 = 0; c0 < ns; c0 += SC_ROWS) {
-        int64_t qrow[SC_ROWS];
         float dl[SC_ROWS];
+        bool use[SC_ROWS];
         uint4 qv[SC_ROWS][NV];
 #pragma unroll
         for (int q = 0; q < SC_ROWS; ++q) {
-          qrow[q] = __shfl_sync(0xffffffffu, my_row, (c0 + q) & 31);
+          use[q] = c0 + q < ns;
+          int64_t qr = __shfl_sync(0xffffffffu, my_row, (c0 + q) & 31);
           dl[q] = __shfl_sync(0xffffffffu, my_dl, (c0 + q) & 31);
-          if (c0 + q >= ns) qrow[q] = -1;
+          qr = use[q] ? qr : 0;
 #pragma unroll
           for (int k = 0; k < NV; ++k) {
             const int v = lane + 32 * k;
-            if (qrow[q] >= 0 && v < nvec) qv[q][k] = Q[qrow[q] * nvec + v];
+            if (v < nvec) qv[q][k] = Q[qr * nvec + v];
           }
         }
 #pragma unroll
-        for (int q = 0; q < SC_ROWS; ++q) {
-          if (qrow[q] < 0) continue;
+        for (int q = 0; q < SC_ROWS; ++q)
 #pragma unroll
           for (int k = 0; k < NV; ++k) {
             const int v = lane + 32 * k;
@@ -689,10 +711,12 @@ csr_scatter_vec_kernel(BwdParams b, const int32_t* __restrict__ row_ptr, const i
               float x[E];
               unpack(qv[q][k], x, (T*)nullptr);
 #pragma unroll
-              for (int e = 0; e < E; ++e) acc[k][e] += dl[q] * x[e];
+              for (int e = 0; e < E; ++e) {
+                const float y = acc[k][e] + dl[q] * x[e];
+                acc[k][e] = use[q] ? y : acc[k][e];
+              }
             }
           }
-        }
       }
     }
 #pragma unroll
