@@ -646,7 +646,33 @@ csr_scatter_vec_kernel(BwdParams b, const int32_t* __restrict__ row_ptr, const i
   for (int64_t d = warp; d < b.nd_rows; d += nwarps) {
     const int32_t a0 = row_ptr[d], n = row_ptr[d + 1] - a0;
     const bool ranked = n <= SC_SEG;
-    if (ranked) {
+    if (n <= 128) {
+      // up to 128 sources: four per lane in registers, each ranked by counting
+      // the smaller ids among all of them, broadcast 32 at a time by shuffles
+      // (no loads or branches in the count; ids are distinct, padding is
+      // INT32_MAX and never smaller)
+      int32_t v[4];
+      int rk[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        v[c] = 32 * c + lane < n ? col_idx[a0 + 32 * c + lane] : INT32_MAX;
+        rk[c] = 0;
+      }
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        if (32 * cc >= n) break;  // warp-uniform
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) {
+          const int32_t y = __shfl_sync(0xffffffffu, v[cc], jj);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) rk[c] += y < v[c] ? 1 : 0;
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        if (32 * c + lane < n) seg[rk[c]] = v[c];
+      __syncwarp();
+    } else if (ranked) {
       // rank each source id by counting smaller ids (ids are distinct)
       for (int i = lane; i < n; i += 32) {
         const int32_t x = col_idx[a0 + i];
