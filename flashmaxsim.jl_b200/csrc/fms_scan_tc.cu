@@ -429,7 +429,7 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     uint32_t aphase = 1;     // flips when aslot wraps to 0
     for (int64_t i = 0;; ++i) {  // queued units, up to the end marker
       const int slot = (int)(i % UQ);
-      if (!ptx::warp_wait(&metaf_bar[slot], (uint32_t)((i / UQ) & 1), &abort_s)) goto done;
+      if (!ptx::all_wait(&metaf_bar[slot], (uint32_t)((i / UQ) & 1), &abort_s)) goto done;
       const UnitMeta& m = meta[slot];
       if (m.valid < 0) break;
       const int rows = m.nq * m.Tq;
@@ -442,7 +442,7 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       if (lane == 0) ptx::mbar_arrive(&metae_bar[slot]);
       if (ARES && anew) {
         if (++aslot == ARES) { aslot = 0; aphase ^= 1; }
-        if (!ptx::warp_wait(&aempty_bar[aslot], aphase ^ 1, &abort_s)) goto done;
+        if (!ptx::all_wait(&aempty_bar[aslot], aphase ^ 1, &abort_s)) goto done;
         if (lane == 0) {
           unsigned char* sA = aslots + aslot * abytes;
           ptx::mbar_expect_tx(&afull_bar[aslot], (uint32_t)(P.KB * nmt * M * ROWB));
@@ -465,7 +465,7 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const int n = min(NT, leff - u0);
         const int nr = (n + 15) & ~15;
         for (int ks = 0; ks < spc; ++ks) {
-          if (!ptx::warp_wait(&empty_bar[stage], phase ^ 1, &abort_s)) goto done;
+          if (!ptx::all_wait(&empty_bar[stage], phase ^ 1, &abort_s)) goto done;
           if (lane == 0) {
             unsigned char* st = ring + stage * sbytes;
             if (ARES) {
@@ -503,7 +503,7 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     uint32_t tph = 0;        // TP: phase of this tile's accumulator barriers
     for (int64_t i = 0;; ++i) {  // queued units, up to the end marker
       const int slot = (int)(i % UQ);
-      if (!ptx::warp_wait(&metaf_bar[slot], (uint32_t)((i / UQ) & 1), &abort_s)) goto done;
+      if (!ptx::all_wait(&metaf_bar[slot], (uint32_t)((i / UQ) & 1), &abort_s)) goto done;
       const UnitMeta& m = meta[slot];
       if (m.valid < 0) break;
       const int rows = m.nq * m.Tq;
@@ -516,7 +516,7 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       if (ARES && anew) {
         if (holding && lane == 0) ptx::mma_commit(&aempty_bar[aslot]);  // after its last MMA
         if (++aslot == ARES) { aslot = 0; aslot_phase ^= 1; }
-        if (!ptx::warp_wait(&afull_bar[aslot], aslot_phase, &abort_s)) goto done;
+        if (!ptx::all_wait(&afull_bar[aslot], aslot_phase, &abort_s)) goto done;
         ptx::tc_fence_after();
         holding = true;
       }
@@ -584,7 +584,7 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     float* scores = static_cast<float*>(p.scores);
     for (int64_t i = 0;; ++i) {  // queued units, up to the end marker
       const int slot = (int)(i % UQ);
-      if (!ptx::warp_wait(&metaf_bar[slot], (uint32_t)((i / UQ) & 1), &abort_s)) goto done;
+      if (!ptx::all_wait(&metaf_bar[slot], (uint32_t)((i / UQ) & 1), &abort_s)) goto done;
       const UnitMeta& m = meta[slot];
       if (m.valid < 0) break;
       const int ub = (int)(i & 1);  // buffer of this unit (red_s, half_*)
@@ -738,7 +738,7 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         }
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(&epi_bar);
-        if (!ptx::warp_wait(&epi_bar, ephase, &abort_s)) goto done;
+        if (!ptx::all_wait(&epi_bar, ephase, &abort_s)) goto done;
         ephase ^= 1;
         if (h == 0 && lr >= 0) {
 #pragma unroll
@@ -800,7 +800,7 @@ tc_scan_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       } else {
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(&epi_bar);
-        if (!ptx::warp_wait(&epi_bar, ephase, &abort_s)) goto done;
+        if (!ptx::all_wait(&epi_bar, ephase, &abort_s)) goto done;
         ephase ^= 1;
         if (et < m.nq) {
           const int qi = et;
