@@ -643,8 +643,9 @@ csr_scatter_vec_kernel(BwdParams b, const int32_t* __restrict__ row_ptr, const i
   const int nvec = p.dim / E;
   const int64_t warp = (int64_t)blockIdx.x * SC_WARPS + w;
   const int64_t nwarps = (int64_t)gridDim.x * SC_WARPS;
-  for (int64_t d = warp; d < b.nd_rows; d += nwarps) {
-    const int32_t a0 = row_ptr[d], n = row_ptr[d + 1] - a0;
+  // one destination: its sources (col_idx[a0 .. a0 + n)) summed in ascending
+  // id order into dD row d
+  auto do_dest = [&](int64_t d, int32_t a0, int32_t n) {
     const bool ranked = n <= SC_SEG;
     if (n <= 128) {
       // up to 128 sources: four per lane in registers, each ranked by counting
@@ -751,6 +752,40 @@ csr_scatter_vec_kernel(BwdParams b, const int32_t* __restrict__ row_ptr, const i
       if (v < nvec) dD[d * nvec + v] = pack(acc[k], (T*)nullptr);
     }
     __syncwarp();
+  };
+  if (b.nd_rows >= 64 * nwarps) {
+    // many destinations per warp (a whole gallery's gradient, mostly empty):
+    // 32 consecutive destinations per step, their row_ptr entries loaded by
+    // the lanes at once, the empty ones written as zero rows without their own
+    // dependent loads, the others summed one by one
+    for (int64_t d0 = warp * 32; d0 < b.nd_rows; d0 += nwarps * 32) {
+      const int64_t dl = d0 + lane;
+      int32_t my_a0 = 0, my_n = 0;
+      if (dl < b.nd_rows) {
+        my_a0 = row_ptr[dl];
+        my_n = row_ptr[dl + 1] - my_a0;
+      }
+      const uint32_t inr = __ballot_sync(0xffffffffu, dl < b.nd_rows);
+      const uint32_t ne = __ballot_sync(0xffffffffu, my_n > 0);
+      uint32_t em = inr & ~ne;
+      while (em) {
+        const int j = __ffs(em) - 1;
+        em &= em - 1;
+#pragma unroll
+        for (int k = 0; k < NV; ++k) {
+          const int v = lane + 32 * k;
+          if (v < nvec) dD[(d0 + j) * nvec + v] = make_uint4(0u, 0u, 0u, 0u);
+        }
+      }
+      uint32_t nm = ne;
+      while (nm) {
+        const int j = __ffs(nm) - 1;
+        nm &= nm - 1;
+        do_dest(d0 + j, __shfl_sync(0xffffffffu, my_a0, j), __shfl_sync(0xffffffffu, my_n, j));
+      }
+    }
+  } else {
+    for (int64_t d = warp; d < b.nd_rows; d += nwarps) do_dest(d, row_ptr[d], row_ptr[d + 1] - row_ptr[d]);
   }
 }
 
