@@ -551,6 +551,80 @@ __device__ __forceinline__ void inb_gather_row(const BwdParams& b, int64_t r, in
   }
 }
 
+// dQ of the other layouts (no atomics): the units of a row are decoded 32 at a
+// time (one per lane: slot, validity, tape entry, delta), then their document
+// rows are summed in ascending unit order with RowsInFlight rows in flight;
+// units that contribute nothing read row 0 and are discarded by a select, so
+// the sum is the one of the one-row-at-a-time kernel, bit for bit.
+template <typename T, int NV>
+__device__ __forceinline__ void gen_gather_row(const BwdParams& b, int64_t r, int lane) {
+  constexpr int E = V16<T>::E;
+  constexpr int R = RowsInFlight<NV>::n;
+  const ScanParams& p = b.g;
+  const uint4* D = static_cast<const uint4*>(p.D);
+  uint4* dQ = static_cast<uint4*>(b.dQ);
+  const int nvec = p.dim / E;
+  int64_t u0, cnt;
+  int t;
+  units_of_row(p, r, u0, cnt, t);
+  float acc[NV][E];
+#pragma unroll
+  for (int k = 0; k < NV; ++k)
+#pragma unroll
+    for (int e = 0; e < E; ++e) acc[k][e] = 0.f;
+  for (int64_t i0 = 0; i0 < cnt; i0 += 32) {
+    int64_t my_row = -1;
+    float my_dl = 0.f;
+    if (i0 + lane < cnt) {
+      int64_t dr;
+      float dl;
+      if (unit_row<T, false>(b, u0 + i0 + lane, 0, i0 + lane, t, dr, dl)) {
+        my_row = dr;
+        my_dl = dl;
+      }
+    }
+    const int nd = (int)min((int64_t)32, cnt - i0);
+#pragma unroll 1
+    for (int c0 = 0; c0 < nd; c0 += R) {
+      float dl[R];
+      bool use[R];
+      uint4 dv[R][NV];
+#pragma unroll
+      for (int q = 0; q < R; ++q) {
+        int64_t dr = __shfl_sync(0xffffffffu, my_row, (c0 + q) & 31);
+        dl[q] = __shfl_sync(0xffffffffu, my_dl, (c0 + q) & 31);
+        use[q] = c0 + q < nd && dr >= 0;
+        dr = use[q] ? dr : 0;
+#pragma unroll
+        for (int k = 0; k < NV; ++k) {
+          const int v = lane + 32 * k;
+          if (v < nvec) dv[q][k] = D[dr * nvec + v];
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < R; ++q)
+#pragma unroll
+        for (int k = 0; k < NV; ++k) {
+          const int v = lane + 32 * k;
+          if (v < nvec) {
+            float x[E];
+            unpack(dv[q][k], x, (T*)nullptr);
+#pragma unroll
+            for (int e = 0; e < E; ++e) {
+              const float y = acc[k][e] + dl[q] * x[e];
+              acc[k][e] = use[q] ? y : acc[k][e];
+            }
+          }
+        }
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int v = lane + 32 * k;
+    if (v < nvec) dQ[r * nvec + v] = pack(acc[k], (T*)nullptr);
+  }
+}
+
 template <typename T, bool ATOMIC, int NV, bool INB>
 __global__ void __launch_bounds__(256, 2) bwd_gather_vec_kernel(BwdParams b, float* dD_acc) {
   constexpr int E = V16<T>::E;
@@ -564,6 +638,8 @@ __global__ void __launch_bounds__(256, 2) bwd_gather_vec_kernel(BwdParams b, flo
   const int nvec = p.dim / E;  // 16-byte vectors per row
   if constexpr (INB && !ATOMIC) {
     for (int64_t r = warp; r < b.nq_rows; r += nwarps) inb_gather_row<T, NV>(b, r, lane);
+  } else if constexpr (!ATOMIC) {
+    for (int64_t r = warp; r < b.nq_rows; r += nwarps) gen_gather_row<T, NV>(b, r, lane);
   } else {
     for (int64_t r = warp; r < b.nq_rows; r += nwarps) {
       int64_t u0, cnt;
@@ -768,6 +844,13 @@ csr_scatter_vec_kernel(BwdParams b, const int32_t* __restrict__ row_ptr, const i
       const uint32_t inr = __ballot_sync(0xffffffffu, dl < b.nd_rows);
       const uint32_t ne = __ballot_sync(0xffffffffu, my_n > 0);
       uint32_t em = inr & ~ne;
+      if (ne == 0u) {
+        // no destination of the step has a source: its rows are one contiguous
+        // block of zeros, written with every lane
+        const int64_t nv = (int64_t)__popc(inr) * nvec;
+        for (int64_t v = lane; v < nv; v += 32) dD[d0 * nvec + v] = make_uint4(0u, 0u, 0u, 0u);
+        continue;
+      }
       while (em) {
         const int j = __ffs(em) - 1;
         em &= em - 1;
