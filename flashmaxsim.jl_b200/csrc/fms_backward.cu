@@ -706,10 +706,10 @@ __global__ void __launch_bounds__(256, 2) bwd_gather_vec_kernel(BwdParams b, flo
 // Warp per destination document token: sources summed in ascending id order.
 
 template <typename T, int NV, bool INB>
-__global__ void __launch_bounds__(SC_WARPS * 32, 2)
+__global__ void __launch_bounds__(SC_WARPS * 32, NV <= 3 ? 3 : 2)
 csr_scatter_vec_kernel(BwdParams b, const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col_idx) {
   constexpr int E = V16<T>::E;
-  constexpr int SC_ROWS = RowsInFlight<NV>::n;
+  constexpr int SC_ROWS = 2;  // rows in flight (up to three blocks per SM share the registers)
   __shared__ int32_t seg_s[SC_WARPS][SC_SEG];
   const ScanParams& p = b.g;
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
