@@ -318,6 +318,145 @@ __global__ void __launch_bounds__(SORT_THREADS) csr_sort_long_kernel(const int32
 
 constexpr int SC_WARPS = 8;
 
+// ------------------------------------------------------------ in-batch CSR
+// The in-batch sources of document j are the pairs (i, t) of the units
+// u = i * Bd + j.  Their ids u * Tq + t ascend with e = i * Tq + t, which is
+// also the query-token row the source reads.  So the CSR of one document is a
+// stable counting sort of its Bq * Tq tape entries by argmax, done by one block
+// in shared memory: the segments come out in ascending source order with no
+// atomics on global memory and no ranking or sorting afterwards, and each
+// entry is stored pre-decoded as (query row, delta) for the scatter.
+constexpr int IB_THREADS = 512;
+constexpr int IB_WARPS = IB_THREADS / 32;
+constexpr int IB_TD_MAX = 1024;    // destinations per document
+constexpr int IB_E_MAX = 16384;    // sources per document (Bq * Tq), keys staged in shared memory
+constexpr int IB_BQ_MAX = 4096;    // deltas of a document's units staged in shared memory
+
+// Destination token (argmax - 1) of source e of document j, or -1 when it
+// contributes nothing (masked query token or no argmax); as source_dest().
+__device__ __forceinline__ int inb_key(const ScanParams& p, int64_t j, int e) {
+  const int i = e / p.Tq;
+  const int t = e - i * p.Tq;
+  const bool qok = p.qmask == nullptr || p.qmask[e] != 0;  // qmask row i, token t
+  const int a = p.args[((int64_t)i * p.Bd + j) * p.Tq + t];
+  return (qok && a >= 1 && a <= p.Td) ? a - 1 : -1;
+}
+
+// Sources of each document (one block per document).
+__global__ void __launch_bounds__(IB_THREADS) inb_csr_total_kernel(ScanParams p, int32_t* __restrict__ doc_tot) {
+  __shared__ int32_t ws[IB_WARPS];
+  const int64_t j = blockIdx.x;
+  const int E = p.Bq * p.Tq;
+  int n = 0;
+#pragma unroll 4
+  for (int e = threadIdx.x; e < E; e += IB_THREADS) n += inb_key(p, j, e) >= 0 ? 1 : 0;
+  n = __reduce_add_sync(0xffffffffu, n);
+  if ((threadIdx.x & 31) == 0) ws[threadIdx.x >> 5] = n;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int t = 0;
+    for (int w = 0; w < IB_WARPS; ++w) t += ws[w];
+    doc_tot[j] = t;
+  }
+}
+
+// Shared memory of inb_csr_build_kernel: per-warp counts [IB_WARPS][Td],
+// segment starts [Td], unit deltas [Bq], source keys [Bq * Tq] (int16).
+static size_t inb_csr_smem(int Td, int Bq, int Tq) {
+  return (size_t)(IB_WARPS + 1) * Td * 4 + (size_t)Bq * 4 + (size_t)Bq * Tq * 2;
+}
+
+// One document per block: its segments (row_ptr) and its sources in
+// ascending order as (query row, delta).  doc_base[j] = sources of the
+// documents before j; the last block also writes row_ptr[Bd * Td].
+template <typename T>
+__global__ void __launch_bounds__(IB_THREADS)
+inb_csr_build_kernel(BwdParams b, const int32_t* __restrict__ doc_base, int32_t* __restrict__ row_ptr,
+                     int32_t* __restrict__ qrow, float* __restrict__ coef) {
+  extern __shared__ int32_t ib_s[];
+  __shared__ int32_t wsum[IB_WARPS];
+  const ScanParams& p = b.g;
+  const int64_t j = blockIdx.x;
+  const int Td = p.Td;
+  const int E = p.Bq * p.Tq;
+  const int per = ((E + IB_WARPS - 1) / IB_WARPS + 31) & ~31;  // sources per warp, whole chunks
+  int32_t* hist = ib_s;                                       // [IB_WARPS][Td]
+  int32_t* bin = hist + IB_WARPS * Td;                        // [Td]
+  float* cq = reinterpret_cast<float*>(bin + Td);             // [Bq]
+  int16_t* key = reinterpret_cast<int16_t*>(cq + p.Bq);       // [E]
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  for (int x = tid; x < IB_WARPS * Td; x += IB_THREADS) hist[x] = 0;
+  for (int i = tid; i < p.Bq; i += IB_THREADS) cq[i] = unit_delta<T>(b, (int64_t)i * p.Bd + j, i);
+  __syncthreads();
+  // pass 1: keys, counted per owning warp (warp w owns sources [w * per, (w + 1) * per))
+#pragma unroll 4
+  for (int e = tid; e < E; e += IB_THREADS) {
+    const int k = inb_key(p, j, e);
+    key[e] = (int16_t)k;
+    if (k >= 0) atomicAdd(&hist[(e / per) * Td + k], 1);
+  }
+  __syncthreads();
+  // pass 2: per destination the warps' counts become running offsets; the
+  // destination totals are scanned (contiguous destinations per thread)
+  const int bpt = (Td + IB_THREADS - 1) / IB_THREADS;
+  const int a0 = min(Td, tid * bpt), a1 = min(Td, a0 + bpt);
+  int mysum = 0;
+  for (int a = a0; a < a1; ++a) {
+    int run = 0;
+    for (int ww = 0; ww < IB_WARPS; ++ww) {
+      const int h = hist[ww * Td + a];
+      hist[ww * Td + a] = run;
+      run += h;
+    }
+    bin[a] = run;
+    mysum += run;
+  }
+  int incl = mysum;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) wsum[w] = incl;
+  __syncthreads();
+  int before = 0, total = 0;
+  for (int ww = 0; ww < IB_WARPS; ++ww) {
+    before += ww < w ? wsum[ww] : 0;
+    total += wsum[ww];
+  }
+  int off = before + incl - mysum;
+  for (int a = a0; a < a1; ++a) {
+    const int n = bin[a];
+    bin[a] = off;
+    off += n;
+  }
+  __syncthreads();
+  const int32_t base = doc_base[j];
+  for (int a = tid; a < Td; a += IB_THREADS) {
+    const int st = bin[a];
+    row_ptr[j * Td + a] = base + st;
+    for (int ww = 0; ww < IB_WARPS; ++ww) hist[ww * Td + a] += st;
+  }
+  if (j == p.Bd - 1 && tid == 0) row_ptr[(int64_t)p.Bd * Td] = base + total;
+  __syncthreads();
+  // pass 3: each warp places its sources in order; lanes with the same
+  // destination take consecutive places in lane order
+  const int e_lo = w * per, e_hi = min(E, e_lo + per);
+  for (int e0 = e_lo; e0 < e_hi; e0 += 32) {
+    const int e = e0 + lane;
+    const int k = e < e_hi ? (int)key[e] : -1;
+    const uint32_t peers = __match_any_sync(0xffffffffu, k >= 0 ? k : 0x100000 + lane);
+    if (k >= 0) {
+      const int pos = base + hist[w * Td + k] + __popc(peers & ((1u << lane) - 1u));
+      qrow[pos] = e;
+      coef[pos] = cq[e / p.Tq];
+    }
+    __syncwarp();
+    if (k >= 0 && lane == __ffs(peers) - 1) hist[w * Td + k] += __popc(peers);
+    __syncwarp();
+  }
+}
+
 // Warp per destination document token; sources summed in ascending id order.
 template <typename T>
 __global__ void __launch_bounds__(SC_WARPS * 32)
@@ -704,10 +843,13 @@ __global__ void __launch_bounds__(256, 2) bwd_gather_vec_kernel(BwdParams b, flo
 }
 
 // Warp per destination document token: sources summed in ascending id order.
+// PRE: the segments are already in ascending order and hold (query row,
+// delta) pairs (col_idx, coef) instead of source ids.
 
-template <typename T, int NV, bool INB>
+template <typename T, int NV, bool INB, bool PRE = false>
 __global__ void __launch_bounds__(SC_WARPS * 32, NV <= 3 ? 3 : 2)
-csr_scatter_vec_kernel(BwdParams b, const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col_idx) {
+csr_scatter_vec_kernel(BwdParams b, const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col_idx,
+                       const float* __restrict__ coef = nullptr) {
   constexpr int E = V16<T>::E;
   constexpr int SC_ROWS = 2;  // rows in flight (up to three blocks per SM share the registers)
   __shared__ int32_t seg_s[SC_WARPS][SC_SEG];
@@ -722,8 +864,8 @@ csr_scatter_vec_kernel(BwdParams b, const int32_t* __restrict__ row_ptr, const i
   // one destination: its sources (col_idx[a0 .. a0 + n)) summed in ascending
   // id order into dD row d
   auto do_dest = [&](int64_t d, int32_t a0, int32_t n) {
-    const bool ranked = n <= SC_SEG;
-    if (n <= 128) {
+    const bool ranked = !PRE && n <= SC_SEG;
+    if (!PRE && n <= 128) {
       // up to 128 sources: four per lane in registers, each ranked by counting
       // the smaller ids among all of them, broadcast 32 at a time by shuffles
       // (no loads or branches in the count; ids are distinct, padding is
@@ -770,7 +912,12 @@ csr_scatter_vec_kernel(BwdParams b, const int32_t* __restrict__ row_ptr, const i
       // in flight
       int64_t my_row = -1;
       float my_dl = 0.f;
-      if (i0 + lane < n) {
+      if (PRE) {
+        if (i0 + lane < n) {
+          my_row = col_idx[a0 + i0 + lane];
+          my_dl = coef[a0 + i0 + lane];
+        }
+      } else if (i0 + lane < n) {
         // source ids are int32 (the CSR stores them so): 32-bit division
         const uint32_t s = (uint32_t)(ranked ? seg[i0 + lane] : col_idx[a0 + i0 + lane]);
         const uint32_t u = s / (uint32_t)p.Tq;
@@ -907,16 +1054,20 @@ static bool launch_gather_vec(const BwdParams& b, float* acc, unsigned grid, cud
   }
   }
 }
+// coef != nullptr: the in-batch CSR of inb_csr_build_kernel (pre-decoded).
 template <typename T>
 static bool launch_scatter_vec(const BwdParams& b, const int32_t* row_ptr, const int32_t* col_idx, unsigned grid,
-                               cudaStream_t s) {
+                               cudaStream_t s, const float* coef = nullptr) {
   if constexpr (sizeof(T) == 8) {
     return false;
   } else {
   switch (vec_lanes<T>(b)) {
 #define FMS_SV(NV)                                                                                   \
   case NV:                                                                                           \
-    if (b.g.layout == L_INBATCH)                                                                     \
+    if (coef != nullptr)                                                                             \
+      csr_scatter_vec_kernel<T, NV, true, true><<<grid, SC_WARPS * 32, 0, s>>>(b, row_ptr, col_idx, \
+                                                                               coef);               \
+    else if (b.g.layout == L_INBATCH)                                                                \
       csr_scatter_vec_kernel<T, NV, true><<<grid, SC_WARPS * 32, 0, s>>>(b, row_ptr, col_idx);      \
     else                                                                                             \
       csr_scatter_vec_kernel<T, NV, false><<<grid, SC_WARPS * 32, 0, s>>>(b, row_ptr, col_idx);     \
@@ -1007,6 +1158,27 @@ static cudaError_t run_backward(int strategy, const BwdParams& b, void* ws, size
   if (!launch_gather_vec<T, false>(b, nullptr, grid_for(b.nq_rows, 8), s))
     bwd_gather_kernel<T, false><<<grid_for(b.nq_rows, 8), 256, 0, s>>>(b, nullptr);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  // in-batch with the vector scatter: per-document stable counting sort
+  // (document totals -> their exclusive scan -> one block per document), the
+  // sources stored as (query row, delta) in col_idx and sort_tmp
+  if (p.layout == L_INBATCH && vec_lanes<T>(b) > 0 && p.Bd >= 1 && p.Td >= 1 && p.Td <= IB_TD_MAX &&
+      p.Bq <= IB_BQ_MAX && (int64_t)p.Bq * p.Tq <= IB_E_MAX && n_dest > 0) {
+    int32_t* doc_base = cursor;  // Bd <= n_dest entries
+    float* coef = reinterpret_cast<float*>(sort_tmp);
+    inb_csr_total_kernel<<<(unsigned)p.Bd, IB_THREADS, 0, s>>>(p, doc_base);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    scan_sums_kernel<<<1, SCAN_BLOCK, 0, s>>>(doc_base, p.Bd);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    const size_t smem = inb_csr_smem(p.Td, p.Bq, p.Tq);
+    if (smem > 48 * 1024 &&
+        (e = cudaFuncSetAttribute(inb_csr_build_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)smem)) != cudaSuccess)
+      return e;
+    inb_csr_build_kernel<T><<<(unsigned)p.Bd, IB_THREADS, smem, s>>>(b, doc_base, row_ptr, col_idx, coef);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    launch_scatter_vec<T>(b, row_ptr, col_idx, grid_for(n_dest, SC_WARPS), s, coef);
+    return cudaGetLastError();
+  }
   // counting sort: counts land at row_ptr[dest], exclusive scan turns them into
   // segment starts, row_ptr[n_dest] = nnz.
   if ((e = cudaMemsetAsync(row_ptr, 0, (size_t)nscan * 4 + 4, s)) != cudaSuccess) return e;

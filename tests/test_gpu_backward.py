@@ -274,3 +274,27 @@ def test_inbatch_invgrid_many_documents(fms, oracle, dtype, dim):
     assert (dQ[~qm] == 0).all()
     dQ2, dD2 = fms.inbatch_pullback(Delta, Q, D, qm, args, None, fms.InvGrid())
     assert torch.equal(dQ, dQ2) and torch.equal(dD, dD2)
+
+
+@pytest.mark.parametrize("dtype,dim,Bq", [(torch.bfloat16, 768, 7), (torch.float16, 64, 9),
+                                          (torch.float32, 96, 5), (torch.bfloat16, 128, 530)])
+def test_inbatch_invgrid_matches_candidates_bitwise(fms, dtype, dim, Bq):
+    """The in-batch InvGrid backward (per-document stable counting sort; for
+    530 queries x 32 tokens, over the per-document staging limit, the general
+    CSR) equals, bit for bit, the candidate backward with every document as a
+    candidate of every query: the same units, deltas and tape in the same
+    ascending source order (backward_layouts.jl:79,146)."""
+    rng = seeded(71 + dim + Bq)
+    Bd, Tq, Td = 37, 32, 50
+    Q, D = feats(rng, (Bq, Tq, dim), dtype), feats(rng, (Bd, Td, dim), dtype)
+    qm = torch.from_numpy(rng.random((Bq, Tq)) > 0.15).cuda()
+    lens = rng.integers(1, Td + 1, Bd)
+    dm = torch.from_numpy(np.arange(Td)[None, :] < lens[:, None]).cuda()
+    _, args = fms.inbatch_forward(Q, D, qm, dm)
+    Delta = torch.randn(Bq, Bd, device="cuda").to(dtype)
+    inv = (torch.rand(Bq, device="cuda") + 0.5).to(dtype)
+    dQ, dD = fms.inbatch_pullback(Delta, Q, D, qm, args, inv, fms.InvGrid())
+    idxs = torch.arange(1, Bd + 1, dtype=torch.int32, device="cuda").repeat(Bq, 1)
+    cQ, cG = fms.candidates_pullback(Delta, Q, D, idxs, qm, args, inv, fms.InvGrid())
+    assert torch.equal(dD, cG)
+    assert torch.equal(dQ, cQ)
