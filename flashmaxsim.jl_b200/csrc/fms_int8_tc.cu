@@ -133,12 +133,14 @@ __device__ __forceinline__ uint32_t tmem_ld1_sync(uint32_t taddr) {
 }
 
 // Max of the dequantised scores of 32 columns (one thread = one query token):
-// s = (qs * ds_u) * (acc_bits - 12582912), paired f32x2, three-input maxima.
+// s = (qs * ds_u) * (acc_bits - 12582912), paired f32x2, three-input maxima
+// into four independent running maxima (two chains of maxima would serialise
+// on the max latency).
 // FULL: every column valid; otherwise the mask word selects (-inf elsewhere).
 // Branch-free: on this part a branch costs more than the selects it skips.
 template <bool FULL>
 __device__ __forceinline__ void reduce32(const uint32_t (&r)[32], uint32_t mm, const float* ds, float2 qs2,
-                                         float& mx0, float& mx1) {
+                                         float (&mx)[4]) {
   const float2 negm = make_float2(-MAGIC_F, -MAGIC_F);
   const float4* dsp = reinterpret_cast<const float4*>(ds);
 #pragma unroll
@@ -148,13 +150,15 @@ __device__ __forceinline__ void reduce32(const uint32_t (&r)[32], uint32_t mm, c
     const float2 a1 = __fadd2_rn(make_float2(__uint_as_float(r[4 * q4 + 2]), __uint_as_float(r[4 * q4 + 3])), negm);
     const float2 s0 = __fmul2_rn(__fmul2_rn(qs2, make_float2(dv.x, dv.y)), a0);
     const float2 s1 = __fmul2_rn(__fmul2_rn(qs2, make_float2(dv.z, dv.w)), a1);
+    float& m0 = mx[2 * (q4 & 1)];
+    float& m1 = mx[2 * (q4 & 1) + 1];
     if (FULL) {
-      mx0 = max3(mx0, s0.x, s0.y);
-      mx1 = max3(mx1, s1.x, s1.y);
+      m0 = max3(m0, s0.x, s0.y);
+      m1 = max3(m1, s1.x, s1.y);
     } else {
       const uint32_t b4 = mm >> (4 * q4);
-      mx0 = max3(mx0, (b4 & 1u) ? s0.x : -INFINITY, (b4 & 2u) ? s0.y : -INFINITY);
-      mx1 = max3(mx1, (b4 & 4u) ? s1.x : -INFINITY, (b4 & 8u) ? s1.y : -INFINITY);
+      m0 = max3(m0, (b4 & 1u) ? s0.x : -INFINITY, (b4 & 2u) ? s0.y : -INFINITY);
+      m1 = max3(m1, (b4 & 4u) ? s1.x : -INFINITY, (b4 & 8u) ? s1.y : -INFINITY);
     }
   }
 }
@@ -165,13 +169,13 @@ __device__ __forceinline__ void reduce32(const uint32_t (&r)[32], uint32_t mm, c
 // registers that 18 warps per SM leave each thread.
 template <int W, bool FULL>
 __device__ __forceinline__ void reduce_doc(uint32_t tcol, const uint32_t* mw, const float* ds, float2 qs2,
-                                           float& mx0, float& mx1) {
+                                           float (&mx)[4]) {
 #pragma unroll 1
   for (int w = 0; w < W; ++w) {
     uint32_t r[32];
     ptx::tmem_ld32(tcol + 32 * w, r);
     tmem_wait_ld_regs(r);
-    reduce32<FULL>(r, FULL ? 0u : mw[w], ds + 32 * w, qs2, mx0, mx1);
+    reduce32<FULL>(r, FULL ? 0u : mw[w], ds + 32 * w, qs2, mx);
   }
 }
 
@@ -394,7 +398,7 @@ i8_exhaustive_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
     const int g = (warp - 2) >> 2;
     const int sp = warp & 3;
     const uint32_t tacc = tmem_base + ((uint32_t)(sp * 32) << 16) + (uint32_t)(g * P.UW);
-    uint32_t c = 0;  // units so far (all groups)
+    uint32_t c = 0;  // units of the stages before this one (all groups)
     for (int64_t i = 0; i < my_st; ++i) {
       const int s = (int)(i & (STAGES - 1));
       const uint32_t ph = (uint32_t)((i / STAGES) & 1);
@@ -403,61 +407,65 @@ i8_exhaustive_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
       int ndoc = P.dps;
       if (j0 + ndoc > P.N) ndoc = (int)(P.N - j0);
       const int nunit = (ndoc + P.dpu - 1) / P.dpu;
-      for (int mt = 0; mt < P.MT; ++mt) {
+      const uint32_t nus = (uint32_t)(P.MT * nunit);  // units of this stage, (M tile, unit) order
+      // this group's units: unit c + k goes to accumulator (c + k) mod 2^nbl
+      // (groups beyond the accumulator count take none)
+      const uint32_t k0 = g < (1 << nbl) ? (((uint32_t)g - c) & ((1u << nbl) - 1u)) : nus;
+      for (uint32_t k = k0; k < nus; k += 1u << nbl) {
+        const int mt = nunit == 2 ? (int)(k >> 1) : (int)(k / (uint32_t)nunit);
+        const int u = (int)k - mt * nunit;
         const int qi = mt * 4 + sp;  // query of this warp within the launch
-        for (int u = 0; u < nunit; ++u, ++c) {
-          if ((int)(c & ((1u << nbl) - 1u)) != g) continue;
-          const uint32_t use = c >> nbl;
-          if (!ptx::all_wait(&accf_bar[g], use & 1u, &abort_s)) goto done;
-          ptx::tc_fence_after();
-          const float qsv = qs_s[qi][lane];
-          const uint32_t qv = qv_s[qi];
-          const bool tv = (qv >> lane) & 1u;
-          const float2 qs2 = make_float2(qsv, qsv);
-          const int d1 = min((u + 1) * P.dpu, ndoc);
-          for (int d = u * P.dpu; d < d1; ++d) {
-            const int first = first_s[s][d];
-            const int cbase = (d - u * P.dpu) * P.Tdp;  // column within the accumulator
-            const int sbase = d * P.Tdp;                // column within the stage
-            float mx0 = -INFINITY, mx1 = -INFINITY;
-            // one warp-uniform test per document: all its columns valid?
-            const uint32_t* mwd = &mw_s[s][d * W];
-            bool full = true;
+        const uint32_t use = (c + k) >> nbl;
+        if (!ptx::all_wait(&accf_bar[g], use & 1u, &abort_s)) goto done;
+        ptx::tc_fence_after();
+        const float qsv = qs_s[qi][lane];
+        const uint32_t qv = qv_s[qi];
+        const bool tv = (qv >> lane) & 1u;
+        const float2 qs2 = make_float2(qsv, qsv);
+        const int d1 = min((u + 1) * P.dpu, ndoc);
+        for (int d = u * P.dpu; d < d1; ++d) {
+          const int first = first_s[s][d];
+          const int cbase = (d - u * P.dpu) * P.Tdp;  // column within the accumulator
+          const int sbase = d * P.Tdp;                // column within the stage
+          float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+          // one warp-uniform test per document: all its columns valid?
+          const uint32_t* mwd = &mw_s[s][d * W];
+          bool full = true;
 #pragma unroll
-            for (int w = 0; w < W; ++w) full = full && mwd[w] == 0xffffffffu;
-            if (full) reduce_doc<W, true>(tacc + cbase, mwd, &ds_s[s][sbase], qs2, mx0, mx1);
-            else reduce_doc<W, false>(tacc + cbase, mwd, &ds_s[s][sbase], qs2, mx0, mx1);
-            const float mx = fmaxf(mx0, mx1);
-            float v = 0.f;
-            if (first >= 0) {
-              // the first valid column is taken unconditionally (a NaN there sticks);
-              // every later column replaces it only when strictly greater.  With
-              // float(acc) finite, that score is NaN only if qs * ds is not finite,
-              // so the accumulator is read back only then.
-              v = mx;
-              const float pf = qsv * ds_s[s][sbase + first];
-              if (__any_sync(0xffffffffu, !isfinite(pf))) {  // warp-uniform: the load is .sync.aligned
-                const uint32_t r0 = tmem_ld1_sync(tacc + cbase + first);
-                const float sf = pf * (__uint_as_float(r0) - MAGIC_F);
-                if (sf != sf) v = sf;
-              }
-            }
-            float sum = (tv && first >= 0) ? v : 0.f;
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-            if (lane == 0 && qi < P.nq) {
-              if (P.normalize) {
-                const int nvalid = __popc(qv);
-                sum = sum * (1.0f / (float)(nvalid > 1 ? nvalid : 1));
-              }
-              P.S[(int64_t)(P.q0 + qi) * P.N + j0 + d] = sum;
+          for (int w = 0; w < W; ++w) full = full && mwd[w] == 0xffffffffu;
+          if (full) reduce_doc<W, true>(tacc + cbase, mwd, &ds_s[s][sbase], qs2, mx4);
+          else reduce_doc<W, false>(tacc + cbase, mwd, &ds_s[s][sbase], qs2, mx4);
+          const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+          float v = 0.f;
+          if (first >= 0) {
+            // the first valid column is taken unconditionally (a NaN there sticks);
+            // every later column replaces it only when strictly greater.  With
+            // float(acc) finite, that score is NaN only if qs * ds is not finite,
+            // so the accumulator is read back only then.
+            v = mx;
+            const float pf = qsv * ds_s[s][sbase + first];
+            if (__any_sync(0xffffffffu, !isfinite(pf))) {  // warp-uniform: the load is .sync.aligned
+              const uint32_t r0 = tmem_ld1_sync(tacc + cbase + first);
+              const float sf = pf * (__uint_as_float(r0) - MAGIC_F);
+              if (sf != sf) v = sf;
             }
           }
-          ptx::tc_fence_before();
-          __syncwarp();
-          if (lane == 0) ptx::mbar_arrive(&acce_bar[g]);
+          float sum = (tv && first >= 0) ? v : 0.f;
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+          if (lane == 0 && qi < P.nq) {
+            if (P.normalize) {
+              const int nvalid = __popc(qv);
+              sum = sum * (1.0f / (float)(nvalid > 1 ? nvalid : 1));
+            }
+            P.S[(int64_t)(P.q0 + qi) * P.N + j0 + d] = sum;
+          }
         }
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&acce_bar[g]);
       }
+      c += nus;
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(&empty_bar[s]);
     }
