@@ -388,11 +388,14 @@ inb_csr_build_kernel(BwdParams b, const int32_t* __restrict__ doc_base, int32_t*
   for (int x = tid; x < IB_WARPS * Td; x += IB_THREADS) hist[x] = 0;
   for (int i = tid; i < p.Bq; i += IB_THREADS) cq[i] = unit_delta<T>(b, (int64_t)i * p.Bd + j, i);
   __syncthreads();
-  // pass 1: keys, counted per owning warp (warp w owns sources [w * per, (w + 1) * per))
-#pragma unroll 4
+  // pass 1: keys (the tape loads of a thread all in flight at once, no
+  // atomics between them), then counted per owning warp (warp w owns sources
+  // [w * per, (w + 1) * per))
+#pragma unroll 8
+  for (int e = tid; e < E; e += IB_THREADS) key[e] = (int16_t)inb_key(p, j, e);
+  __syncthreads();
   for (int e = tid; e < E; e += IB_THREADS) {
-    const int k = inb_key(p, j, e);
-    key[e] = (int16_t)k;
+    const int k = key[e];
     if (k >= 0) atomicAdd(&hist[(e / per) * Td + k], 1);
   }
   __syncthreads();

@@ -126,3 +126,38 @@ def test_fused_query_quantisation_matches(fms, oracle, qdt, nq, Tq, Td, dim, N):
     So = oracle.int8_exhaustive(QQ.codes, QQ.scales.float(), index.codes, index.scales,
                                 qm.cpu(), dm.cpu())
     assert_scores(S.cpu(), So, 1e-5)
+
+
+def test_exhaustive_tc_half_documents_masks_nan(fms, oracle):
+    """128-token document slots run in two 64-column halves: masks that leave
+    only one half (or part of it) valid, a first valid column in either half,
+    a NaN scale in the first valid column of either half (it sticks) and after
+    it (it never wins), normalize on and off."""
+    rng = seeded(65)
+    nq, Tq, Td, dim, N = 6, 24, 128, 128, 300
+    Q, index = _case(fms, rng, nq, Tq, Td, dim, N)
+    qmask = torch.from_numpy(rng.random((nq, Tq)) > 0.25).cuda()
+    dmask = torch.from_numpy(rng.random((N, Td)) > 0.3).cuda()
+    dmask[7] = False                       # empty document -> 0
+    dmask[8] = False
+    dmask[8, 90:] = True                   # first valid column 90 (second half)
+    dmask[9] = False
+    dmask[9, 0] = True                     # only token 0
+    dmask[10] = False
+    dmask[10, 70:] = True                  # first valid column 70 ...
+    dmask[11] = True
+    dmask[12] = True
+    dmask[13] = False
+    dmask[13, 40:64] = True                # first half only
+    scales = index.scales.clone()
+    scales[10, 70] = float("nan")          # ... with a NaN scale: sticks
+    scales[11, 0] = float("nan")           # NaN in the first column of the first half: sticks
+    scales[12, 100] = float("nan")         # NaN after the first valid column: never wins
+    index = fms.Int8Index(index.codes, scales)
+    for normalize in (False, True):
+        S = fms.int8_exhaustive_forward(Q, index, qmask, dmask, normalize=normalize)
+        So = _oracle_S(fms, oracle, Q, index, qmask, dmask, normalize=normalize)
+        live = qmask.any(1).cpu().numpy()
+        assert np.isnan(So[live][:, [10, 11]]).all() and not np.isnan(So[:, 12]).any()
+        assert_scores(S.cpu(), So, 1e-5)
+    assert torch.all(S[:, 7] == 0)
