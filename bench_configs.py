@@ -404,7 +404,8 @@ def run_c3(args, world, rank, local, dev, fms):
     line["e2e"] = {"value": world * args.steps / (te / 1e3), "unit": "steps/s",
                    "h2d_bytes_per_step": Q.numel() * 2 + D.numel() * 2 + dmask.numel() + dS.numel() * 4,
                    "d2h_bytes_per_step": BQ3 * BD3 * 4}
-    line["gpu_launches"] = None
+    nl = B.count_launches(lambda: step(lambda *_: None), dev)
+    line["gpu_launches"] = None if nl is None else nl * args.steps
     line["roofline"] = {"bound": "tensor", "achieved": achieved, "peak": pk["bf16"],
                         "unit": "TFLOP/s", "frac": achieved / pk["bf16"], "traffic": None,
                         "peak_source": f"{pk['src']} bf16_tflops (burst; the kernel is timed alone)",
@@ -483,7 +484,8 @@ def run_c3_sharded(args, world, rank, local, dev, fms):
                           "all-reduce(sum) of dQ in float32")
     line = base_line(args, world, "in-batch fwd+bwd steps/sec", args.steps / (ms / 1e3), "steps/s",
                      ms_step, "bf16", cfg, scaling="weak")
-    line["gpu_launches"] = None
+    nl = B.count_launches(lambda: step(lambda *_: None), dev)
+    line["gpu_launches"] = None if nl is None else nl * args.steps
     line["roofline"] = {"bound": "tensor", "note": "per-rank forward as in the 1-GPU line",
                         "fwd_ms": parts.get("fwd", 0) / args.steps,
                         "bwd_ms": parts.get("bwd", 0) / args.steps}
@@ -758,7 +760,8 @@ def run_c5(args, world, rank, local, dev, fms):
     line["config"]["doc_tokens_per_step"] = tot_tok
     line["e2e"] = {"value": tot_tok * args.steps / (te / 1e3), "unit": UNIT_TOK,
                    "h2d_bytes_per_step": Qh.numel() * 2, "d2h_bytes_per_step": NQ5 * K5 * 8}
-    line["gpu_launches"] = None
+    nl = B.count_launches(lambda: step(lambda *_: None), dev)
+    line["gpu_launches"] = None if nl is None else nl * args.steps
     line["roofline"] = {"bound": "tensor", "achieved": achieved, "peak": int8_peak,
                         "unit": "TOP/s", "frac": achieved / int8_peak, "traffic": None,
                         "peak_source": f"2 x {pk['src']} bf16_tflops (B200 dense int8 rate is "
