@@ -237,28 +237,69 @@ __device__ void bitonic_desc(uint64_t* a, int n) {
   __syncthreads();
 }
 
-constexpr int TOPK_CHUNK = 8192;  // keys sorted per block (64 KB shared memory)
+constexpr int TOPK_CHUNK = 8192;  // keys per block and round (64 KB shared memory)
+constexpr int TOPK_THREADS = 1024;
+constexpr int TOPK_PER = TOPK_CHUNK / TOPK_THREADS;  // keys per thread
+constexpr int TOPK_PRUNE_K = TOPK_THREADS / TOPK_PER;  // k up to which a chunk is pruned first
 
 // One reduction round: every chunk of TOPK_CHUNK keys of a query's list keeps its
 // best k.  From S (first round, keys built from scores and ids) or from keys.
-__global__ void __launch_bounds__(1024) topk_round_kernel(const float* __restrict__ S,
-                                                          const uint64_t* __restrict__ kin,
-                                                          int64_t L, int nq, int k,
-                                                          int64_t id_offset,
-                                                          uint64_t* __restrict__ kout) {
+// Keys are unique (the id is part of the key) and 0 only as padding.
+//
+// For k <= TOPK_PRUNE_K the chunk is pruned before it is sorted: with t the
+// k-th largest of the threads' maxima, at least k keys are >= t, so every key
+// of the chunk's best k is >= t; and only a thread whose maximum is >= t can
+// hold such a key, so at most TOPK_PER * k <= TOPK_THREADS nonzero keys
+// survive (if fewer than k threads hold a nonzero key, t = 0 and the
+// survivors are all the nonzero keys, fewer still).  Sorting the 1024 maxima
+// and the 1024 survivors replaces the sort of all 8192 keys; the result is the
+// same best k in the same order.
+__global__ void __launch_bounds__(TOPK_THREADS) topk_round_kernel(const float* __restrict__ S,
+                                                                 const uint64_t* __restrict__ kin,
+                                                                 int64_t L, int nq, int k,
+                                                                 int64_t id_offset,
+                                                                 uint64_t* __restrict__ kout) {
   extern __shared__ uint64_t keys[];
+  __shared__ int nsurv;
   const int64_t nchunks = (L + TOPK_CHUNK - 1) / TOPK_CHUNK;
   for (int64_t job = blockIdx.x; job < nchunks * nq; job += gridDim.x) {
     const int64_t c = job % nchunks, qi = job / nchunks;
     const int64_t j0 = c * TOPK_CHUNK;
     __syncthreads();
-    for (int i = threadIdx.x; i < TOPK_CHUNK; i += blockDim.x) {
-      int64_t j = j0 + i;
-      uint64_t key = 0ull;
-      if (j < L) key = S ? topk_key(S[j + L * qi], (uint32_t)(j + 1 + id_offset)) : kin[qi * L + j];
-      keys[i] = key;
+    if (k <= TOPK_PRUNE_K) {
+      uint64_t kv[TOPK_PER];
+      uint64_t mx = 0ull;
+#pragma unroll
+      for (int r = 0; r < TOPK_PER; ++r) {
+        const int64_t j = j0 + threadIdx.x + (int64_t)r * TOPK_THREADS;
+        uint64_t key = 0ull;
+        if (j < L) key = S ? topk_key(S[j + L * qi], (uint32_t)(j + 1 + id_offset)) : kin[qi * L + j];
+        kv[r] = key;
+        mx = key > mx ? key : mx;
+      }
+      keys[threadIdx.x] = mx;
+      if (threadIdx.x == 0) nsurv = 0;
+      bitonic_desc(keys, TOPK_THREADS);  // ends with a block barrier
+      const uint64_t t = keys[k - 1];
+      __syncthreads();
+#pragma unroll
+      for (int r = 0; r < TOPK_PER; ++r)
+        if (kv[r] != 0ull && kv[r] >= t) {
+          const int pos = atomicAdd(&nsurv, 1);
+          if (pos < TOPK_THREADS) keys[pos] = kv[r];  // always, by the bound above
+        }
+      __syncthreads();
+      for (int i = min(nsurv, TOPK_THREADS) + threadIdx.x; i < TOPK_THREADS; i += TOPK_THREADS) keys[i] = 0ull;
+      bitonic_desc(keys, TOPK_THREADS);
+    } else {
+      for (int i = threadIdx.x; i < TOPK_CHUNK; i += blockDim.x) {
+        int64_t j = j0 + i;
+        uint64_t key = 0ull;
+        if (j < L) key = S ? topk_key(S[j + L * qi], (uint32_t)(j + 1 + id_offset)) : kin[qi * L + j];
+        keys[i] = key;
+      }
+      bitonic_desc(keys, TOPK_CHUNK);
     }
-    bitonic_desc(keys, TOPK_CHUNK);
     for (int i = threadIdx.x; i < k; i += blockDim.x)
       kout[(qi * nchunks + c) * k + i] = keys[i];
   }
@@ -304,7 +345,7 @@ cudaError_t launch_topk(const float* S, int64_t N, int nq, int k, int64_t id_off
   // Rounds until a single chunk remains; each round shrinks L by TOPK_CHUNK/k >= 2.
   while (true) {
     int64_t jobs = ((L + TOPK_CHUNK - 1) / TOPK_CHUNK) * nq;
-    topk_round_kernel<<<(unsigned)(jobs < cap ? jobs : cap), 1024, smem, s>>>(
+    topk_round_kernel<<<(unsigned)(jobs < cap ? jobs : cap), TOPK_THREADS, smem, s>>>(
         first ? S : nullptr, in, L, nq, k, id_offset, out);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     int64_t Ln = topk_round_len(L, k);

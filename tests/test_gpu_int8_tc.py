@@ -161,3 +161,28 @@ def test_exhaustive_tc_half_documents_masks_nan(fms, oracle):
         assert np.isnan(So[live][:, [10, 11]]).all() and not np.isnan(So[:, 12]).any()
         assert_scores(S.cpu(), So, 1e-5)
     assert torch.all(S[:, 7] == 0)
+
+
+@pytest.mark.parametrize("k", [1, 100, 128, 129, 300])
+def test_topk_equals_stable_sort_of_the_scan_scores(fms, k):
+    """Top-k of the exhaustive search = the first k of the scan's own scores
+    sorted by score descending, then document id ascending, bit for bit, over
+    several chunks and rounds of the selection: 40,000 documents, a block of
+    100 copies of one document (equal scores, ranked by id) and 3,000 empty
+    documents (score 0).  k <= 128 prunes each chunk before sorting it."""
+    rng = seeded(66)
+    nq, Tq, Td, dim, N = 5, 16, 32, 128, 40000
+    Q, index = _case(fms, rng, nq, Tq, Td, dim, N)
+    codes, scales = index.codes.clone(), index.scales.clone()
+    codes[100:200] = codes[5]
+    scales[100:200] = scales[5]
+    index = fms.Int8Index(codes, scales)
+    dmask = torch.ones((N, Td), dtype=torch.bool, device="cuda")
+    dmask[20000:23000] = False
+    vals, ids, S = fms.int8_exhaustive_forward(Q, index, None, dmask, topk=k, return_scores=True)
+    S = S.cpu().numpy()
+    did = np.arange(1, N + 1)
+    for qi in range(nq):
+        order = np.lexsort((did, -S[qi].astype(np.float64)))[:k]
+        assert np.array_equal(ids[qi].cpu().numpy(), did[order]), qi
+        assert np.array_equal(vals[qi].cpu().numpy(), S[qi][order]), qi
