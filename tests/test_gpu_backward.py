@@ -298,3 +298,20 @@ def test_inbatch_invgrid_matches_candidates_bitwise(fms, dtype, dim, Bq):
     cQ, cG = fms.candidates_pullback(Delta, Q, D, idxs, qm, args, inv, fms.InvGrid())
     assert torch.equal(dD, cG)
     assert torch.equal(dQ, cQ)
+
+
+def test_inbatch_invgrid_large_documents_bitwise(fms):
+    """600-token documents and 512 queries x 32 tokens: the per-document CSR
+    build needs more than 48 KB of shared memory (the opt-in launch); equal
+    bit for bit to the candidate backward with every document a candidate."""
+    rng = seeded(77)
+    Bq, Bd, Tq, Td, dim = 512, 3, 32, 600, 64
+    dtype = torch.float16
+    Q, D = feats(rng, (Bq, Tq, dim), dtype), feats(rng, (Bd, Td, dim), dtype)
+    _, args = fms.inbatch_forward(Q, D)
+    Delta = torch.randn(Bq, Bd, device="cuda").to(dtype)
+    dQ, dD = fms.inbatch_pullback(Delta, Q, D, None, args, None, fms.InvGrid())
+    idxs = torch.arange(1, Bd + 1, dtype=torch.int32, device="cuda").repeat(Bq, 1)
+    cQ, cG = fms.candidates_pullback(Delta, Q, D, idxs, None, args, None, fms.InvGrid())
+    assert torch.equal(dD, cG)
+    assert torch.equal(dQ, cQ)
